@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""bench.py -- MoE-layer throughput of the B200-native hot path.
+
+Default workload (N=1): BASELINE config 3 -- one MoE layer over 16384 tokens,
+hidden 2048, 32 experts, top-4, expert SwiGLU intermediate 1792, bf16 expert
+weights with fp32 accumulation, router logits drawn so that per-expert load
+follows Zipf(s=1.1) (injected exactly through the inputs: gate = [I_32 | 0],
+x[:, :32] = ln p_e + Gumbel noise; the router GEMM still runs over all 2048
+columns).  One step = one full layer forward (route, scan, scatter, W1/W3
+SwiGLU grouped GEMM, W2 grouped GEMM, combine) on inputs resident in HBM.
+
+With --gpus N (launched under torchrun) every rank runs the same layer on its
+own 16384 tokens (independent replicas; expert-parallel exchange is not part
+of this line), value = all ranks' tokens / max-over-ranks device time.
+
+--impl reference times the reference's own implementation of the path on the
+box's host cores (the C restatement in oracle/, since the reference ships no
+CPU implementation of this path), on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, E, K, I = 2048, 32, 4, 1792
+T_DEFAULT = 16384
+ZIPF_S = 1.1
+SEED = 1234
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
+    p.add_argument("--tokens", type=int, default=T_DEFAULT)
+    p.add_argument("--dtype", choices=["bf16", "tf32"], default="bf16")
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="target CPU work of the bounded cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"],
+                    bf16_sustained=d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, smi_index):
+        self.idx = smi_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if self.idx is None:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        os.remove(self.path)
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows)
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+                if any(r[3].replace(".", "").isdigit() for r in rows) else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def smi_index_for(dev_index: int):
+    """nvidia-smi index of torch device `dev_index` (matched by PCI bus id)."""
+    import torch
+    try:
+        props = torch.cuda.get_device_properties(dev_index)
+        bus = getattr(props, "pci_bus_id", None)
+        dom = getattr(props, "pci_domain_id", 0)
+        out = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id",
+                              "--format=csv,noheader"], capture_output=True, text=True,
+                             timeout=30).stdout
+        if bus is not None:
+            for line in out.strip().splitlines():
+                idx, pci = [s.strip() for s in line.split(",")]
+                # pci like 00000000:1B:00.0
+                b = int(pci.split(":")[1], 16)
+                d = int(pci.split(":")[0], 16)
+                if b == bus and d == dom:
+                    return int(idx)
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return int(vis.split(",")[dev_index])
+        return dev_index
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ inputs
+def make_inputs(T, routing, dev, seed=SEED):
+    """x [T,H] fp32, gate [E,H] fp32, fp32 expert weights -- generated on the device."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, H, device=dev, generator=g)
+    if routing == "zipf":
+        p = torch.arange(1, E + 1, dtype=torch.float64, device=dev) ** (-ZIPF_S)
+        p = p / p.sum()
+        u = torch.rand(T, E, device=dev, generator=g, dtype=torch.float64).clamp_min(1e-300)
+        L = (p.log()[None, :] - torch.log(-torch.log(u))).float()
+        gate = torch.zeros(E, H, device=dev)
+        gate[torch.arange(E), torch.arange(E)] = 1.0
+        x[:, :E] = L
+        bias = None
+    else:
+        gate = torch.randn(E, H, device=dev, generator=g) * 0.02
+        bias = torch.randn(E, device=dev, generator=g) * 0.02
+    w1 = torch.randn(E, I, H, device=dev, generator=g) * 0.02
+    w3 = torch.randn(E, I, H, device=dev, generator=g) * 0.02
+    w2 = torch.randn(E, H, I, device=dev, generator=g) * 0.02
+    return x, gate, bias, w1, w2, w3
+
+
+def layer_flop(T):
+    return T * (2 * H * E + K * (4 * H * I + 2 * I * H))
+
+
+# ------------------------------------------------------------------ ours
+def run_ours(args, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+    from final_b200 import SparseMoeBlock, launch_count
+
+    T = args.tokens
+    x, gate, bias, w1, w2, w3 = make_inputs(T, args.routing, dev, SEED + rank)
+    layer = SparseMoeBlock(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype)
+    w_host = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # fp32 weights for the CPU baseline sample (same workload)
+        w_host = [t.cpu().numpy() for t in (w1, w3, w2)]
+        cpu_inputs = (x.cpu().numpy(), gate.cpu().numpy(),
+                      None if bias is None else bias.cpu().numpy())
+    del w1, w2, w3
+    torch.cuda.empty_cache()
+    y = torch.empty(T, H, device=dev)
+    counts_probe = layer.forward_traced(x)["counts"].cpu().tolist()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        layer.forward_gpu(x, y, 1, T, H, stream)
+    torch.cuda.synchronize()
+    st = layer.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status 0x{st:x} after warm-up")
+
+    sampler = ClockSampler(smi_index_for(dev.index))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    layer.profile(True)
+    n0 = launch_count()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        layer.forward_gpu(x, y, 1, T, H, stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    n1 = launch_count()
+    layer.profile(False)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    stage_ms, nfw = layer.profile_read()
+    st = layer.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status 0x{st:x} in timed region")
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+
+    # ---- end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        yh = torch.empty(T, H, dtype=torch.float32).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(2):
+            xd.copy_(xh, non_blocking=True)
+            layer.forward_gpu(xd, y, 1, T, H, stream)
+            yh.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            xd.copy_(xh, non_blocking=True)
+            layer.forward_gpu(xd, y, 1, T, H, stream)
+            yh.copy_(y, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = t.item()
+        e2e = {"value": T * args.steps * world / (ems / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+               "ms_per_step": ems / args.steps}
+
+    pk = peaks()
+    flop = layer_flop(T)
+    value = T * args.steps * world / (ms / 1e3)
+    gemm_flop = T * K * 6 * H * I
+    w13_flop = T * K * 4 * H * I
+    w13_ms = stage_ms["gemm_w13"] / max(nfw, 1)
+    w2_ms = stage_ms["gemm_w2"] / max(nfw, 1)
+    achieved = w13_flop / (w13_ms / 1e3) / 1e12
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "gemm_w13_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            traffic = json.load(f).get("bytes_per_launch_scaled")
+
+    out = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": {"workload": f"moe_layer_{T // 1024}k_{args.routing}", "tokens_per_gpu": T,
+                   "hidden": H, "experts": E, "top_k": K, "inter": I,
+                   "routing": ("zipf(1.1) injected logits" if args.routing == "zipf"
+                               else "x.gate N(0,1)xN(0,0.02), bias N(0,0.02)"),
+                   "expert_load_max_min": [max(counts_probe), min(counts_probe)],
+                   "weights": f"{args.dtype} packed from fp32 N(0,0.02)",
+                   "l2": "inputs larger than L2: x 134 MB fp32, expert weights 705 MB bf16",
+                   "parallelism": "replicas" if world > 1 else "single"},
+        "layer_tflops": flop * args.steps * world / (ms / 1e3) / 1e12 / world,
+        "grouped_gemm_tflops": gemm_flop / ((w13_ms + w2_ms) / 1e3) / 1e12,
+        "frac_of_bf16_peak_layer": flop / (ms / args.steps / 1e3) / 1e12 / pk["bf16"],
+        "stages_ms_per_step": {k: v / max(nfw, 1) for k, v in stage_ms.items()},
+        "roofline": {"kernel": "gemm_sm100_kernel<SwiGLU,bf16> (W1||W3 grouped GEMM)",
+                     "bound": "tensor", "achieved": achieved,
+                     "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_sustained"], "traffic": traffic,
+                     "peak_kind": f"{pk['source']} sustained bf16 (burst {pk['bf16']})",
+                     "flop_per_launch": w13_flop},
+        "gpu_launches": int(n1 - n0),
+        "clocks": clocks,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    if w_host is not None:
+        out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
+    return out
+
+
+# ------------------------------------------------------------------ CPU
+def cpu_sample_rate(x, gate, bias, w1, w3, w2, target_s, max_tokens=None):
+    """Time the oracle (C restatement of the reference MoE, all host threads)
+    on growing token samples until ~target_s of work; returns tokens/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    o.lib()
+    threads = o.num_threads()
+    n = 16
+    best = None
+    while True:
+        xs = x[:n]
+        t0 = time.perf_counter()
+        o.moe_forward(xs, gate, bias, w1, w2, w3, K=K)
+        dt = time.perf_counter() - t0
+        best = (n, dt)
+        if dt * 3 > target_s or (max_tokens and n * 2 > max_tokens) or n * 2 > x.shape[0]:
+            break
+        n *= 2
+    n, dt = best
+    return n / dt, n, dt, threads
+
+
+def cpu_baseline(args, cpu_inputs, w_host):
+    x, gate, bias = cpu_inputs
+    w1, w3, w2 = w_host
+    rate, n, dt, threads = cpu_sample_rate(x, gate, bias, w1, w3, w2, args.cpu_seconds)
+    return {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} tokens of the same workload (fp32 oracle, {dt:.1f} s)"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's MoE semantics on the host cores."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    T = args.tokens
+    dev = torch.device("cuda:0") if torch.cuda.is_available() else None
+    if dev is not None:
+        x, gate, bias, w1, w2, w3 = make_inputs(T, args.routing, dev)
+        xc, gc = x.cpu().numpy(), gate.cpu().numpy()
+        bc = None if bias is None else bias.cpu().numpy()
+        w1c, w3c, w2c = (t.cpu().numpy() for t in (w1, w3, w2))
+    else:
+        inp = o.moe_inputs(T, H, E, I, SEED, bias=args.routing != "zipf")
+        xc, gc, bc = inp["x"], inp["gate"], inp["bias"]
+        if args.routing == "zipf":
+            o.inject_logits(xc, gc, o.zipf_logits(T, E, SEED))
+        w1c, w3c, w2c = inp["w1"], inp["w3"], inp["w2"]
+    o.lib()
+    threads = o.num_threads()
+    # bounded sample per step: size it so warmup+steps take a few minutes at most
+    budget_s = max(20.0, min(150.0, 8.0 * (args.steps + args.warmup)))
+    per_step = budget_s / (args.steps + args.warmup)
+    _, n, _, _ = cpu_sample_rate(xc, gc, bc, w1c, w3c, w2c, per_step)
+    rng = np.random.default_rng(0)
+    for _ in range(args.warmup):
+        s = int(rng.integers(0, T - n + 1))
+        o.moe_forward(xc[s:s + n], gc, bc, w1c, w2c, w3c, K=K)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s = int(rng.integers(0, T - n + 1))
+        o.moe_forward(xc[s:s + n], gc, bc, w1c, w2c, w3c, K=K)
+    dt = time.perf_counter() - t0
+    value = n * args.steps / dt
+    out = {"impl": "reference", "metric": "moe_layer_tokens_per_s", "value": value,
+           "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": f"moe_layer_{T // 1024}k_{args.routing}", "tokens_per_gpu": T,
+                      "hidden": H, "experts": E, "top_k": K, "inter": I},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                            "sample": f"{n} tokens per step of the {T}-token workload "
+                                      "(C restatement of src/layer.cu MoE, fp32, OpenMP)"},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    if dev is not None:
+        out["reference_cuda_kernels_b200"] = ref_gpu_kernels(args, x, gate, bias, w1, w2, w3, dev)
+    return out
+
+
+def ref_gpu_kernels(args, x, gate, bias, w1, w2, w3, dev):
+    """The reference's own fp32 CUDA kernels (compiled unmodified for sm_100a,
+    oracle/_ref) launched as SparseMoeBlock::forward_gpu does, same workload."""
+    import ctypes as C
+    import torch
+    import oracle as o
+    r = o.ref_lib()
+    if r is None:
+        return {"unavailable": "oracle/_ref not built"}
+    T = x.shape[0]
+    arr = C.c_void_p * E
+    p1 = arr(*[w1[e].data_ptr() for e in range(E)])
+    p2 = arr(*[w2[e].data_ptr() for e in range(E)])
+    p3 = arr(*[w3[e].data_ptr() for e in range(E)])
+    h = C.c_void_p()
+    vp = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+    if r.ref_moe_create(C.cast(p1, C.c_void_p), C.cast(p2, C.c_void_p), C.cast(p3, C.c_void_p),
+                        vp(gate), vp(bias), E, K, H, I, T, 288, C.byref(h)) != 0:
+        return {"unavailable": "ref_moe_create failed"}
+    y = torch.empty(T, H, device=dev)
+    z = [None] * 7
+    for _ in range(2):
+        r.ref_moe_forward(h, vp(x), vp(y), T, *z, None)
+    torch.cuda.synchronize()
+    steps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        r.ref_moe_forward(h, vp(x), vp(y), T, *z, None)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    r.ref_moe_destroy(h)
+    return {"value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "what": "reference kernels (fp32 FFMA, 288 persistent CTAs as shipped) on this B200"}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+    if args.warmup < 3:
+        args.warmup = 3
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    try:
+        out = run_ours(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

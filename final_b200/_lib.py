@@ -1,0 +1,84 @@
+"""ctypes binding of the C ABI declared in include/b2moe.h.
+
+The CUDA library is mandatory: importing this module on a machine where
+``final_b200/lib/libb2moe.so`` is missing raises immediately -- there is no
+CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2moe.so"
+
+B2_OK, B2_ERR_INVALID, B2_ERR_CUDA, B2_ERR_CAPACITY, B2_ERR_DEVICE, B2_ERR_NO_DEVICE = range(6)
+B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
+
+# Every symbol include/b2moe.h declares (checked by tests/test_abi.py).
+EXPORTED = (
+    "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
+    "b2_moe_get_status", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
+    "b2_kernel_launch_count", "b2_status_string", "b2_version",
+)
+
+
+class B2Error(RuntimeError):
+    def __init__(self, status: int, what: str, lib=None):
+        msg = lib.b2_status_string(status).decode() if lib is not None else str(status)
+        super().__init__(f"{what}: {msg} (status {status})")
+        self.status = status
+
+
+class MoeDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("num_experts", C.c_int),
+                ("top_k", C.c_int), ("max_tokens", C.c_int), ("routed_scale", C.c_float),
+                ("use_bias", C.c_int), ("dtype", C.c_int)]
+
+
+class MoeTrace(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "logits", "topk_idx", "topk_w", "counts", "offsets", "mtile_offsets",
+        "token_slot", "sorted_token", "sorted_w")]
+
+
+_lib = None
+
+
+def load(path: Path | None = None):
+    """Load (once) and type the library; raises if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(
+            f"{p} is missing: build it with `python -m final_b200.build` "
+            "(the MoE / GEMM path has no CPU fallback)")
+    lib = C.CDLL(str(p))
+    vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
+    lib.b2_moe_create.argtypes = [C.POINTER(MoeDesc), vp, vp, vp, vp, vp, i, vp, C.POINTER(vp)]
+    lib.b2_moe_destroy.argtypes = [vp]
+    lib.b2_moe_forward.argtypes = [vp, vp, vp, i, vp]
+    lib.b2_moe_forward_ex.argtypes = [vp, vp, vp, i, C.POINTER(MoeTrace), vp]
+    lib.b2_moe_get_status.argtypes = [vp, vp, C.POINTER(i)]
+    lib.b2_moe_profile_enable.argtypes = [vp, i]
+    lib.b2_moe_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(i)]
+    lib.b2_moe_device_bytes.argtypes = [vp]
+    lib.b2_moe_device_bytes.restype = sz
+    lib.b2_gemm_nt.argtypes = [vp, vp, vp, i, i, i, i, i, vp, vp]
+    lib.b2_convert_f32_to_bf16.argtypes = [vp, vp, sz, vp]
+    lib.b2_kernel_launch_count.restype = C.c_uint64
+    lib.b2_status_string.argtypes = [i]
+    lib.b2_status_string.restype = C.c_char_p
+    lib.b2_version.restype = C.c_char_p
+    for name in ("b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
+                 "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
+                 "b2_moe_profile_enable", "b2_moe_profile_read"):
+        getattr(lib, name).restype = i
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != B2_OK:
+        raise B2Error(status, what, _lib)

@@ -1,0 +1,76 @@
+"""Build recipe for the in-tree CUDA library ``final_b200/lib/libb2moe.so``.
+
+The library is compiled for sm_100a only (tcgen05 / TMA / TMEM code) with an
+explicit ``-gencode arch=compute_100a,code=sm_100a`` and links the CUDA
+runtime statically, so the .so that travels with the repository needs no
+runtime lookup beyond the NVIDIA driver.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIBDIR = PKG / "lib"
+LIB = LIBDIR / "libb2moe.so"
+
+NVCC = os.environ.get("NVCC", "nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+         "--expt-relaxed-constexpr"]
+
+SOURCES = ["b2moe_api.cu"]
+
+
+def _needs_rebuild(target: Path, deps) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(Path(d).stat().st_mtime > t for d in deps)
+
+
+def _deps():
+    out = []
+    for p in list(CSRC.rglob("*.cu")) + list(CSRC.rglob("*.cuh")) + list(CSRC.rglob("*.h")):
+        out.append(p)
+    out += list((ROOT / "include").glob("*.h"))
+    return out
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every .cu of the library into one shared object (in-tree)."""
+    LIBDIR.mkdir(exist_ok=True)
+    if not force and not _needs_rebuild(LIB, _deps()):
+        return LIB
+    objs = []
+    for src in SOURCES:
+        obj = LIBDIR / (Path(src).stem + ".o")
+        cmd = [NVCC, *ARCH, *FLAGS, "-c", str(CSRC / src), "-o", str(obj)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        objs.append(str(obj))
+    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *objs, "-cudart", "static"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    for o in objs:
+        os.remove(o)
+    return LIB
+
+
+def build_oracle(verbose: bool = False) -> None:
+    """Build the CPU oracle (and oracle/_ref when the reference tree exists)."""
+    cmd = ["make", "-C", str(ROOT / "oracle")]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True, stdout=None if verbose else subprocess.DEVNULL)
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    build_oracle(verbose=True)

@@ -1,0 +1,533 @@
+// b2moe_api.cu -- implementation of the C ABI in include/b2moe.h.
+//
+// Owns the packed weights, the scratch buffers and the TMA descriptors of an
+// MoE layer object, and launches the kernel pipeline of moe_kernels.cuh and
+// gemm_sm100.cuh.  Host code only: no torch types, no hidden host syncs on
+// the forward path.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/b2moe.h"
+#include "gemm_sm100.cuh"
+#include "moe_kernels.cuh"
+
+using namespace b2;
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+#define B2_CUDA(call)                                                                  \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess) {                                                           \
+      fprintf(stderr, "[b2moe] %s failed at %s:%d: %s\n", #call, __FILE__, __LINE__,   \
+              cudaGetErrorString(e_));                                                 \
+      return B2_ERR_CUDA;                                                              \
+    }                                                                                  \
+  } while (0)
+
+#define B2_LAUNCHED()                                  \
+  do {                                                 \
+    g_launches.fetch_add(1, std::memory_order_relaxed); \
+    B2_CUDA(cudaGetLastError());                       \
+  } while (0)
+
+// ------------------------------------------------------------ driver entry
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major tile map with 128-byte swizzle: inner dim = k (elements),
+// outer = rows.  box = {128 bytes of k, box_rows}.
+bool make_tmap(CUtensorMap *m, const void *base, bool fp32, uint64_t inner, uint64_t rows,
+               uint64_t row_stride_bytes, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {fp32 ? 32u : 64u, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct DevInfo {
+  int sms = 0;
+  int cc_major = 0;
+};
+
+bool dev_info(DevInfo *d) {
+  int dev;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return false;
+  if (cudaDeviceGetAttribute(&d->cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return false;
+  return true;
+}
+
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
+                      int grid, cudaStream_t s) {
+  auto kern = gemm_sm100_kernel<EPI, TF32, TOut>;
+  const size_t smem = gemm_smem_bytes();
+  // per-device attribute; cheap enough to set on every launch
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (grid <= 0) return B2_OK;
+  kern<<<grid, kGemmThreads, smem, s>>>(ta, tb, args);
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- MoE object
+struct b2_moe {
+  b2_moe_desc d;
+  int device = 0;
+  int Ip = 0;  // inter padded to 128
+  int sms = 0;
+  bool tf32 = false;
+  size_t bytes = 0;
+  // weights
+  float *gateT = nullptr;
+  float *bias = nullptr;
+  void *w13 = nullptr;  // [E][2Ip][H]
+  void *w2 = nullptr;   // [E][H][Ip]
+  // scratch
+  int *topk_idx = nullptr, *block_counts = nullptr, *block_base = nullptr;
+  int *counts = nullptr, *offsets = nullptr, *mtile = nullptr;
+  int *token_slot = nullptr, *sorted_token = nullptr;
+  float *topk_w = nullptr, *sorted_w = nullptr;
+  void *sorted_x = nullptr, *inter = nullptr, *sout = nullptr;
+  int *status = nullptr;
+  CUtensorMap tm_x, tm_w13, tm_inter, tm_w2;
+  std::vector<void *> allocs;
+  // stage profiling
+  bool profile = false;
+  std::vector<cudaEvent_t> ev_pool;   // free events
+  std::vector<cudaEvent_t> ev_rec;    // kStageEvents per recorded forward
+};
+
+static constexpr int kStageEvents = 7;
+
+static cudaEvent_t prof_event(b2_moe *m) {
+  if (!m->ev_pool.empty()) {
+    cudaEvent_t e = m->ev_pool.back();
+    m->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+static void prof_mark(b2_moe *m, cudaStream_t s) {
+  if (!m->profile) return;
+  cudaEvent_t e = prof_event(m);
+  cudaEventRecord(e, s);
+  m->ev_rec.push_back(e);
+}
+
+static b2_status moe_alloc(b2_moe *m, void **p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  B2_CUDA(cudaMalloc(p, bytes));
+  m->allocs.push_back(*p);
+  m->bytes += bytes;
+  return B2_OK;
+}
+
+static void moe_free_all(b2_moe *m) {
+  for (void *p : m->allocs) cudaFree(p);
+  m->allocs.clear();
+  for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->ev_rec) cudaEventDestroy(e);
+  m->ev_pool.clear();
+  m->ev_rec.clear();
+}
+
+extern "C" b2_status b2_moe_destroy(b2_moe *moe) {
+  if (!moe) return B2_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(moe->device);
+  moe_free_all(moe);
+  cudaSetDevice(prev);
+  delete moe;
+  return B2_OK;
+}
+
+#define B2_TRY(x)                      \
+  do {                                 \
+    b2_status s_ = (x);                \
+    if (s_ != B2_OK) {                 \
+      b2_moe_destroy(m);               \
+      return s_;                       \
+    }                                  \
+  } while (0)
+
+extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *w1,
+                                   const float *const *w2, const float *const *w3,
+                                   const float *gate, const float *bias, int weights_on_host,
+                                   b2_stream stream_, b2_moe **out) {
+  if (!desc || !w1 || !w2 || !w3 || !gate || !out) return B2_ERR_INVALID;
+  *out = nullptr;
+  const b2_moe_desc &d = *desc;
+  if (d.hidden <= 0 || d.hidden % 64 != 0 || d.inter <= 0 || d.inter % 16 != 0 ||
+      d.num_experts < 1 || d.num_experts > kMaxExperts || d.top_k < 1 || d.top_k > kMaxTopK ||
+      d.top_k > d.num_experts || d.max_tokens < 1 || (d.dtype != B2_BF16 && d.dtype != B2_TF32))
+    return B2_ERR_INVALID;
+  if (d.use_bias && !bias) return B2_ERR_INVALID;
+  DevInfo di;
+  if (!dev_info(&di)) return B2_ERR_NO_DEVICE;
+  if (di.cc_major != 10) return B2_ERR_NO_DEVICE;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+
+  b2_moe *m = new b2_moe();
+  m->d = d;
+  cudaGetDevice(&m->device);
+  m->sms = di.sms;
+  m->tf32 = d.dtype == B2_TF32;
+  const int E = d.num_experts, H = d.hidden, I = d.inter, K = d.top_k;
+  m->Ip = (I + 127) / 128 * 128;
+  const int Ip = m->Ip;
+  const size_t es = m->tf32 ? 4 : 2;
+  const size_t T = (size_t)d.max_tokens, R = T * K;
+  const size_t nb = (T + kRouteTB - 1) / kRouteTB;
+
+  B2_TRY(moe_alloc(m, (void **)&m->gateT, sizeof(float) * H * kMaxExperts));
+  B2_TRY(moe_alloc(m, (void **)&m->bias, sizeof(float) * kMaxExperts));
+  B2_TRY(moe_alloc(m, &m->w13, es * (size_t)E * 2 * Ip * H));
+  B2_TRY(moe_alloc(m, &m->w2, es * (size_t)E * H * Ip));
+  B2_TRY(moe_alloc(m, (void **)&m->topk_idx, sizeof(int) * R));
+  B2_TRY(moe_alloc(m, (void **)&m->topk_w, sizeof(float) * R));
+  B2_TRY(moe_alloc(m, (void **)&m->block_counts, sizeof(int) * nb * kMaxExperts));
+  B2_TRY(moe_alloc(m, (void **)&m->block_base, sizeof(int) * nb * kMaxExperts));
+  B2_TRY(moe_alloc(m, (void **)&m->counts, sizeof(int) * kMaxExperts));
+  B2_TRY(moe_alloc(m, (void **)&m->offsets, sizeof(int) * kMaxExperts));
+  B2_TRY(moe_alloc(m, (void **)&m->mtile, sizeof(int) * (kMaxExperts + 1)));
+  B2_TRY(moe_alloc(m, (void **)&m->token_slot, sizeof(int) * R));
+  B2_TRY(moe_alloc(m, (void **)&m->sorted_token, sizeof(int) * R));
+  B2_TRY(moe_alloc(m, (void **)&m->sorted_w, sizeof(float) * R));
+  B2_TRY(moe_alloc(m, &m->sorted_x, es * R * H));
+  B2_TRY(moe_alloc(m, &m->inter, es * R * Ip));
+  B2_TRY(moe_alloc(m, &m->sout, es * R * H));
+  B2_TRY(moe_alloc(m, (void **)&m->status, sizeof(int)));
+  if (cudaMemsetAsync(m->status, 0, sizeof(int), stream) != cudaSuccess ||
+      cudaMemsetAsync(m->bias, 0, sizeof(float) * kMaxExperts, stream) != cudaSuccess ||
+      cudaMemsetAsync(m->inter, 0, es * R * Ip, stream) != cudaSuccess) {
+    b2_moe_destroy(m);
+    return B2_ERR_CUDA;
+  }
+
+  // ---- weights: stage host matrices through one expert-sized device buffer
+  float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr, *stg = nullptr;
+  auto fail = [&](b2_status s) {
+    if (st1) cudaFree(st1);
+    if (st3) cudaFree(st3);
+    if (st2) cudaFree(st2);
+    if (stg) cudaFree(stg);
+    b2_moe_destroy(m);
+    return s;
+  };
+  const size_t mat = (size_t)I * H;
+  if (weights_on_host) {
+    if (cudaMalloc(&st1, mat * 4) != cudaSuccess || cudaMalloc(&st3, mat * 4) != cudaSuccess ||
+        cudaMalloc(&st2, mat * 4) != cudaSuccess ||
+        cudaMalloc(&stg, sizeof(float) * E * H) != cudaSuccess)
+      return fail(B2_ERR_CUDA);
+  }
+  for (int e = 0; e < E; ++e) {
+    const float *p1 = w1[e], *p3 = w3[e], *p2 = w2[e];
+    if (!p1 || !p2 || !p3) return fail(B2_ERR_INVALID);
+    if (weights_on_host) {
+      if (cudaMemcpyAsync(st1, p1, mat * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+          cudaMemcpyAsync(st3, p3, mat * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+          cudaMemcpyAsync(st2, p2, mat * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess)
+        return fail(B2_ERR_CUDA);
+      p1 = st1;
+      p3 = st3;
+      p2 = st2;
+    }
+    if (m->tf32) {
+      float *o13 = reinterpret_cast<float *>(m->w13) + (size_t)e * 2 * Ip * H;
+      float *o2 = reinterpret_cast<float *>(m->w2) + (size_t)e * H * Ip;
+      pack_w13_single<float><<<2 * Ip, 256, 0, stream>>>(p1, p3, H, I, Ip, o13);
+      pack_w2_single<float><<<H, 256, 0, stream>>>(p2, H, I, Ip, o2);
+    } else {
+      __nv_bfloat16 *o13 = reinterpret_cast<__nv_bfloat16 *>(m->w13) + (size_t)e * 2 * Ip * H;
+      __nv_bfloat16 *o2 = reinterpret_cast<__nv_bfloat16 *>(m->w2) + (size_t)e * H * Ip;
+      pack_w13_single<__nv_bfloat16><<<2 * Ip, 256, 0, stream>>>(p1, p3, H, I, Ip, o13);
+      pack_w2_single<__nv_bfloat16><<<H, 256, 0, stream>>>(p2, H, I, Ip, o2);
+    }
+    if (cudaGetLastError() != cudaSuccess) return fail(B2_ERR_CUDA);
+    g_launches.fetch_add(2, std::memory_order_relaxed);
+    if (weights_on_host && cudaStreamSynchronize(stream) != cudaSuccess)
+      return fail(B2_ERR_CUDA);  // staging buffers are reused by the next expert
+  }
+  const float *gsrc = gate;
+  if (weights_on_host) {
+    if (cudaMemcpyAsync(stg, gate, sizeof(float) * E * H, cudaMemcpyHostToDevice, stream) !=
+        cudaSuccess)
+      return fail(B2_ERR_CUDA);
+    gsrc = stg;
+  }
+  pack_gate_kernel<<<(H * kMaxExperts + 255) / 256, 256, 0, stream>>>(gsrc, E, H, m->gateT);
+  if (cudaGetLastError() != cudaSuccess) return fail(B2_ERR_CUDA);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (d.use_bias &&
+      cudaMemcpyAsync(m->bias, bias, sizeof(float) * E,
+                      weights_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                      stream) != cudaSuccess)
+    return fail(B2_ERR_CUDA);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return fail(B2_ERR_CUDA);
+  if (st1) cudaFree(st1);
+  if (st3) cudaFree(st3);
+  if (st2) cudaFree(st2);
+  if (stg) cudaFree(stg);
+  st1 = st3 = st2 = stg = nullptr;
+
+  // ---- TMA descriptors (buffers are fixed for the object's lifetime)
+  const bool f = m->tf32;
+  if (!make_tmap(&m->tm_x, m->sorted_x, f, H, R, (uint64_t)H * es, kBM) ||
+      !make_tmap(&m->tm_w13, m->w13, f, H, (uint64_t)E * 2 * Ip, (uint64_t)H * es, kBN) ||
+      !make_tmap(&m->tm_inter, m->inter, f, Ip, R, (uint64_t)Ip * es, kBM) ||
+      !make_tmap(&m->tm_w2, m->w2, f, Ip, (uint64_t)E * H, (uint64_t)Ip * es, kBN)) {
+    b2_moe_destroy(m);
+    return B2_ERR_CUDA;
+  }
+  *out = m;
+  return B2_OK;
+}
+
+static b2_status copy_trace(void *dst, const void *src, size_t bytes, cudaStream_t s) {
+  if (!dst || bytes == 0) return B2_OK;
+  B2_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s));
+  return B2_OK;
+}
+
+extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int T,
+                                       const b2_moe_trace *tr, b2_stream stream_) {
+  if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
+  if (T == 0) return B2_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden, Ip = m->Ip;
+  const int nb = (T + kRouteTB - 1) / kRouteTB;
+  const bool f = m->tf32;
+
+  prof_mark(m, s);
+  route_kernel<<<nb, 64, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E, K,
+                                 m->d.routed_scale, m->topk_idx, m->topk_w, m->block_counts,
+                                 tr ? tr->logits : nullptr);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+  scan_kernel<<<1, 1024, 0, s>>>(m->block_counts, nb, E, kBM, m->counts, m->offsets, m->mtile,
+                                 m->block_base);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+  if (f)
+    scatter_kernel<float><<<nb, 32 * K, 0, s>>>(
+        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
+        reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token, m->sorted_w,
+        m->status);
+  else
+    scatter_kernel<__nv_bfloat16><<<nb, 32 * K, 0, s>>>(
+        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
+        reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot, m->sorted_token,
+        m->sorted_w, m->status);
+  B2_LAUNCHED();
+
+  const long long R = (long long)T * K;
+  const int mt_ub = (int)((R + kBM - 1) / kBM) + E;  // each expert adds <= 1 partial tile
+
+  GemmArgs a1{};
+  a1.counts = m->counts;
+  a1.offsets = m->offsets;
+  a1.mtile_offsets = m->mtile;
+  a1.num_groups = E;
+  a1.b_rows_per_group = 2 * Ip;
+  a1.N = Ip;
+  a1.num_n_tiles = Ip / 128;
+  a1.num_k_blocks = f ? H / 32 : H / 64;
+  a1.out = m->inter;
+  a1.ldo = Ip;
+  a1.status = m->status;
+  const int grid1 = (int)std::min<long long>(m->sms, (long long)mt_ub * a1.num_n_tiles);
+  b2_status st;
+  prof_mark(m, s);
+  if (f)
+    st = launch_gemm<kEpiSwiGLU, true, float>(m->tm_x, m->tm_w13, a1, grid1, s);
+  else
+    st = launch_gemm<kEpiSwiGLU, false, __nv_bfloat16>(m->tm_x, m->tm_w13, a1, grid1, s);
+  if (st != B2_OK) return st;
+
+  GemmArgs a2 = a1;
+  a2.b_rows_per_group = H;
+  a2.N = H;
+  a2.num_n_tiles = (H + kBN - 1) / kBN;
+  a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
+  a2.out = m->sout;
+  a2.ldo = H;
+  const int grid2 = (int)std::min<long long>(m->sms, (long long)mt_ub * a2.num_n_tiles);
+  prof_mark(m, s);
+  if (f)
+    st = launch_gemm<kEpiStore, true, float>(m->tm_inter, m->tm_w2, a2, grid2, s);
+  else
+    st = launch_gemm<kEpiStore, false, __nv_bfloat16>(m->tm_inter, m->tm_w2, a2, grid2, s);
+  if (st != B2_OK) return st;
+
+  prof_mark(m, s);
+  if (f)
+    combine_kernel<float><<<T, 256, 0, s>>>(reinterpret_cast<const float *>(m->sout),
+                                            m->token_slot, m->topk_w, T, H, K, y);
+  else
+    combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(m->sout), m->token_slot, m->topk_w, T, H, K, y);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+
+  if (tr) {
+    const size_t tk = (size_t)T * K;
+    b2_status c = B2_OK;
+    if (c == B2_OK) c = copy_trace(tr->topk_idx, m->topk_idx, tk * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->topk_w, m->topk_w, tk * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->counts, m->counts, (size_t)E * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->offsets, m->offsets, (size_t)E * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->mtile_offsets, m->mtile, (size_t)(E + 1) * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->token_slot, m->token_slot, tk * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->sorted_token, m->sorted_token, tk * 4, s);
+    if (c == B2_OK) c = copy_trace(tr->sorted_w, m->sorted_w, tk * 4, s);
+    if (c != B2_OK) return c;
+  }
+  return B2_OK;
+}
+
+extern "C" b2_status b2_moe_forward(b2_moe *m, const float *x, float *y, int T,
+                                    b2_stream stream) {
+  return b2_moe_forward_ex(m, x, y, T, nullptr, stream);
+}
+
+extern "C" b2_status b2_moe_get_status(b2_moe *m, b2_stream stream_, int *device_status) {
+  if (!m || !device_status) return B2_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  int v = 0;
+  B2_CUDA(cudaStreamSynchronize(s));
+  B2_CUDA(cudaMemcpy(&v, m->status, sizeof(int), cudaMemcpyDeviceToHost));
+  B2_CUDA(cudaMemset(m->status, 0, sizeof(int)));
+  *device_status = v;
+  return v ? B2_ERR_DEVICE : B2_OK;
+}
+
+extern "C" b2_status b2_moe_profile_enable(b2_moe *m, int enable) {
+  if (!m) return B2_ERR_INVALID;
+  m->profile = enable != 0;
+  return B2_OK;
+}
+
+extern "C" b2_status b2_moe_profile_read(b2_moe *m, float *stage_ms, int *forwards) {
+  if (!m || !stage_ms || !forwards) return B2_ERR_INVALID;
+  for (int i = 0; i < kStageEvents - 1; ++i) stage_ms[i] = 0.0f;
+  const size_t n = m->ev_rec.size() / kStageEvents;
+  for (size_t f = 0; f < n; ++f) {
+    cudaEvent_t *ev = &m->ev_rec[f * kStageEvents];
+    B2_CUDA(cudaEventSynchronize(ev[kStageEvents - 1]));
+    for (int i = 0; i < kStageEvents - 1; ++i) {
+      float ms = 0.0f;
+      B2_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+      stage_ms[i] += ms;
+    }
+  }
+  *forwards = (int)n;
+  for (cudaEvent_t e : m->ev_rec) m->ev_pool.push_back(e);
+  m->ev_rec.clear();
+  return B2_OK;
+}
+
+extern "C" size_t b2_moe_device_bytes(const b2_moe *m) { return m ? m->bytes : 0; }
+
+// ---------------------------------------------------------------- dense GEMM
+extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, int N, int K,
+                                int ldc, int dtype, int *status, b2_stream stream_) {
+  if (M < 0 || N <= 0 || K <= 0 || ldc < N || (M > 0 && (!A || !B || !C)))
+    return B2_ERR_INVALID;
+  if (dtype != B2_BF16 && dtype != B2_TF32) return B2_ERR_INVALID;
+  const bool f = dtype == B2_TF32;
+  if (K % (f ? 4 : 8) != 0) return B2_ERR_INVALID;
+  if (M == 0) return B2_OK;
+  DevInfo di;
+  if (!dev_info(&di)) return B2_ERR_NO_DEVICE;
+  const size_t es = f ? 4 : 2;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, A, f, K, M, (uint64_t)K * es, kBM) ||
+      !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, kBN))
+    return B2_ERR_INVALID;
+  GemmArgs g{};
+  g.num_groups = 0;
+  g.M = M;
+  g.N = N;
+  g.num_n_tiles = (N + kBN - 1) / kBN;
+  g.num_k_blocks = (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes);
+  g.group_m = 16;
+  g.out = C;
+  g.ldo = ldc;
+  g.status = status;
+  const long long tiles = (long long)((M + kBM - 1) / kBM) * g.num_n_tiles;
+  const int grid = (int)std::min<long long>(di.sms, tiles);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  if (f) return launch_gemm<kEpiStore, true, float>(ta, tb, g, grid, s);
+  return launch_gemm<kEpiStore, false, float>(ta, tb, g, grid, s);
+}
+
+extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,
+                                            b2_stream stream_) {
+  if (n == 0) return B2_OK;
+  if (!in || !out || (reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return B2_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  const size_t blocks = std::min<size_t>((n / 8 + 255) / 256 + 1, 148 * 16);
+  f32_to_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(in, reinterpret_cast<__nv_bfloat16 *>(out), n);
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
+extern "C" uint64_t b2_kernel_launch_count(void) { return g_launches.load(); }
+
+extern "C" const char *b2_status_string(b2_status s) {
+  switch (s) {
+    case B2_OK: return "ok";
+    case B2_ERR_INVALID: return "invalid argument";
+    case B2_ERR_CUDA: return "CUDA error";
+    case B2_ERR_CAPACITY: return "token count exceeds capacity";
+    case B2_ERR_DEVICE: return "device-side error recorded";
+    case B2_ERR_NO_DEVICE: return "no sm_100 device";
+  }
+  return "unknown";
+}
+
+extern "C" const char *b2_version(void) { return "b2moe sm_100a tcgen05 v0.1"; }

@@ -1,0 +1,348 @@
+// gemm_sm100.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[rows, n] = A[rows, K] . B[n, K]^T        (both operands K-major)
+//
+// One CTA per SM walks a static round-robin list of 128x256 output tiles:
+//   warp 0      TMA producer (one elected lane): A/B k-blocks of 128 bytes
+//               (64 bf16 or 32 fp32) into a 4-stage SW128 smem ring;
+//   warp 1      TMEM allocator + UMMA issuer (one lane): 4 x (128x256xK16/K8)
+//               MMAs per k-block into a double-buffered fp32 TMEM accumulator
+//               (2 x 256 columns), tcgen05.commit frees smem stages;
+//   warps 2..5  epilogue: tcgen05.ld 32x32b of the warp's TMEM lane quarter,
+//               fused SwiGLU / bf16 / fp32 conversion, vector stores.
+//
+// Two schedules share the kernel:
+//   grouped  (MoE experts): rows of A are expert segments [offsets[e],
+//            offsets[e]+counts[e]) of the scattered activations, cut into
+//            128-row tiles by the prefix mtile_offsets[]; tile order is
+//            (expert, m-tile, n-tile) with n fastest, so the tiles in flight
+//            share one expert's weights in L2.  B rows of expert e start at
+//            e * b_rows_per_group.
+//   dense    one group of M rows, rastered in bands of group_m m-tiles so a
+//            band's A tiles and the B tiles in flight stay L2-resident.
+// This replaces the reference's FFMA kernels attn_matmul_tiled_kernel
+// (src/layer.cu:9-141), moe_persistent_fused_w1w3_kernel (:773-972) and
+// moe_persistent_w2_kernel (:974-1126).
+#pragma once
+#include "sm100_ptx.cuh"
+
+namespace b2 {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBKBytes = 128;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBKBytes;  // 16 KB
+constexpr int kBBytes = kBN * kBKBytes;  // 32 KB
+constexpr int kMaxGroups = 256;
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 512;
+
+enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1 };
+
+struct GemmArgs {
+  const int *counts;         // grouped: rows per group
+  const int *offsets;        // grouped: first row of each group in A / C
+  const int *mtile_offsets;  // grouped: exclusive prefix of ceil(count/128), [G+1]
+  int num_groups;            // grouped: G (<= kMaxGroups); dense: 0
+  int b_rows_per_group;      // grouped: rows of B per group
+  int M;                     // dense rows
+  int N;                     // output columns (SwiGLU: gated output columns)
+  int num_n_tiles;
+  int num_k_blocks;
+  int group_m;               // dense raster band height (m-tiles)
+  void *out;
+  long long ldo;             // output row stride in elements
+  int *status;
+};
+
+constexpr size_t gemm_smem_bytes() {
+  return 1024 + (size_t)kStages * (kABytes + kBBytes) + 256 + 3 * (kMaxGroups + 1) * 4;
+}
+
+struct TileInfo {
+  int a_row, b_row, rows_valid, n_tile, cols_valid;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
+                                                const int *s_mt, const int *s_off,
+                                                const int *s_cnt, int out_tile_cols) {
+  TileInfo t;
+  const int NT = g.num_n_tiles;
+  if (g.num_groups > 0) {
+    const int gm = tile / NT;
+    const int n = tile - gm * NT;
+    int lo = 0, hi = g.num_groups;  // s_mt[lo] <= gm < s_mt[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_mt[mid] <= gm) lo = mid; else hi = mid;
+    }
+    const int m = gm - s_mt[lo];
+    t.a_row = s_off[lo] + m * kBM;
+    t.rows_valid = min(kBM, s_cnt[lo] - m * kBM);
+    t.b_row = lo * g.b_rows_per_group + n * kBN;
+    t.n_tile = n;
+  } else {
+    const int MT = (g.M + kBM - 1) / kBM;
+    const int band = g.group_m * NT;
+    const int b = tile / band;
+    const int m0 = b * g.group_m;
+    const int gh = min(g.group_m, MT - m0);
+    const int idx = tile - b * band;
+    const int n = idx / gh;
+    const int m = m0 + (idx - n * gh);
+    t.a_row = m * kBM;
+    t.rows_valid = min(kBM, g.M - t.a_row);
+    t.b_row = n * kBN;
+    t.n_tile = n;
+  }
+  t.cols_valid = min(out_tile_cols, g.N - t.n_tile * out_tile_cols);
+  return t;
+}
+
+// Waits that must complete even while the CTA is aborting (draining our own
+// asynchronous copies / MMAs before the CTA's smem and TMEM are released).
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int *status) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (status) atomicCAS(status, 0, (int)kDevTimeoutDrain);
+      return;
+    }
+  }
+}
+
+// Store up to 32 consecutive fp32 values of one output row as TOut.
+template <typename TOut>
+__device__ __forceinline__ void store_cols(TOut *dst, const float (&h)[32], int valid,
+                                           bool vec_ok) {
+  if (valid <= 0) return;
+  if (valid >= 32 && vec_ok) {
+    if constexpr (sizeof(TOut) == 2) {
+      uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        d[v] = make_uint4(pack_bf16(h[8 * v], h[8 * v + 1]), pack_bf16(h[8 * v + 2], h[8 * v + 3]),
+                          pack_bf16(h[8 * v + 4], h[8 * v + 5]), pack_bf16(h[8 * v + 6], h[8 * v + 7]));
+    } else {
+      float4 *d = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) d[v] = make_float4(h[4 * v], h[4 * v + 1], h[4 * v + 2], h[4 * v + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < valid) {
+        if constexpr (sizeof(TOut) == 2) dst[i] = __float2bfloat16_rn(h[i]);
+        else dst[i] = h[i];
+      }
+  }
+}
+
+template <int EPI, bool TF32, typename TOut>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + kStages * kABytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + kStages * kBBytes);
+  // bars[0..S) full, [S..2S) empty, 2S..2S+1 tmem_full, 2S+2..2S+3 tmem_empty, 2S+4 drain
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  int *s_mt = reinterpret_cast<int *>(bars) + 64;  // 256 B past the barrier block
+  int *s_off = s_mt + (kMaxGroups + 1);
+  int *s_cnt = s_off + (kMaxGroups + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[kStages + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * kStages + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * kStages + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[2 * kStages + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  if (g.num_groups > 0) {
+    for (int i = threadIdx.x; i <= g.num_groups; i += blockDim.x) {
+      s_mt[i] = g.mtile_offsets[i];
+      if (i < g.num_groups) {
+        s_off[i] = g.offsets[i];
+        s_cnt[i] = g.counts[i];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int NT = g.num_n_tiles;
+  const int total_tiles = g.num_groups > 0
+                              ? s_mt[g.num_groups] * NT
+                              : ((g.M + kBM - 1) / kBM) * NT;
+  constexpr int out_tile_cols = (EPI == kEpiSwiGLU) ? kBN / 2 : kBN;
+  const int KB = g.num_k_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      const uint64_t pol = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      uint32_t last_par = 0;
+      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+        const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, out_tile_cols);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, g.status,
+                         kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), kABytes + kBBytes);
+          const int kc = kb * (TF32 ? 32 : 64);
+          tma_load_2d(smem_u32(sA + stage * kABytes), &tmA, full_bar(stage), kc, t.a_row, pol);
+          tma_load_2d(smem_u32(sB + stage * kBBytes), &tmB, full_bar(stage), kc, t.b_row, pol);
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // our own copies must have landed before the CTA may exit
+      for (int s = 0; s < kStages; ++s)
+        if (issued >> s & 1) mbar_drain(full_bar(s), (last_par >> s) & 1, g.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ UMMA issuer
+      constexpr uint32_t idesc = make_idesc(TF32 ? 2u : 1u, kBM, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_par = 0;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1, abort_flag, g.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, g.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a0 = make_sw128_desc(smem_u32(sA + stage * kABytes));
+          const uint64_t b0 = make_sw128_desc(smem_u32(sB + stage * kBBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // +32 bytes per K step inside the 128-byte swizzle atom (>>4 = 2)
+            if (TF32)
+              umma_tf32(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0);
+            else
+              umma_f16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0);
+          }
+          issued_any = true;
+          umma_commit(empty_bar(stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_par ^= 1;
+      }
+      if (issued_any) {
+        umma_commit(drain_bar);
+        mbar_drain(drain_bar, 0, g.status);
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    // 16-byte vector stores need 16-byte aligned rows
+    const bool vec_ok = (g.ldo * (long long)sizeof(TOut)) % 16 == 0;
+    int acc = 0;
+    uint32_t acc_par = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, out_tile_cols);
+      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+        const bool row_ok = row < t.rows_valid;
+      TOut *out = reinterpret_cast<TOut *>(g.out) + (long long)(t.a_row + row) * g.ldo +
+                  (long long)t.n_tile * out_tile_cols;
+      if constexpr (EPI == kEpiSwiGLU) {
+        // columns [0,128) of the accumulator are gate (W1), [128,256) up (W3)
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t gr[32], ur[32];
+          tmem_ld32(tbase + c * 32, gr);
+          tmem_ld32(tbase + 128 + c * 32, ur);
+          tmem_ld_wait();
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gv = __uint_as_float(gr[i]);
+            h[i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(ur[i]);
+          }
+          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) h[i] = __uint_as_float(r[i]);
+          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_par ^= 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b2

@@ -1,0 +1,103 @@
+"""Dense NT GEMM on the tcgen05 core against an fp64 PyTorch reference of the
+same op (C = A . B^T), and against the reference engine's own tiled kernel
+(attn_matmul_tiled_kernel, src/layer.cu:9-141) when oracle/_ref is built.
+
+Tolerances (max |C - C_ref| / max |C_ref|):
+  bf16 operands, fp32 accumulate vs fp64 of the same bf16 values: 1e-4
+      (only the accumulation order differs)
+  bf16 / tf32 vs the reference's fp32 result on fp32 inputs: 1e-2
+      (the north-star tolerance for bf16/TF32 tensor-core math)
+"""
+import ctypes as C
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (128, 256, 64),
+    (200, 300, 128),      # ragged M and N, one partial k-block
+    (512, 2048, 2048),    # out projection, M=512
+    (384, 3072, 2048),    # fused QKV width
+    (64, 65536, 2048),    # LM head, batch rows only
+    (1, 512, 2048),       # single row
+    (1000, 520, 1032),    # K not a multiple of the 64-wide k-block
+]
+
+
+def _rel(a, b):
+    return ((a.double() - b.double()).abs().max() / b.double().abs().max().clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_bf16_vs_fp64(cuda_dev, M, N, K):
+    from final_b200 import gemm_nt
+    g = torch.Generator(device=cuda_dev).manual_seed(M * 7 + N * 3 + K)
+    A = torch.randn(M, K, device=cuda_dev, generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    Cm = gemm_nt(A, B, dtype="bf16", status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = A.double() @ B.double().T
+    assert _rel(Cm, ref) < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:5])
+def test_gemm_tf32_vs_fp64(cuda_dev, M, N, K):
+    from final_b200 import gemm_nt
+    g = torch.Generator(device=cuda_dev).manual_seed(M + N + K)
+    A = torch.randn(M, K, device=cuda_dev, generator=g)
+    B = torch.randn(N, K, device=cuda_dev, generator=g) * 0.02
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    Cm = gemm_nt(A, B, dtype="tf32", status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = A.double() @ B.double().T
+    assert _rel(Cm, ref) < 1e-2
+
+
+def test_gemm_ldc_and_stream(cuda_dev):
+    """Output written with a row stride > N on a side stream leaves the gap untouched."""
+    from final_b200 import gemm_nt
+    M, N, K = 256, 512, 256
+    A = torch.randn(M, K, device=cuda_dev).to(torch.bfloat16)
+    B = torch.randn(N, K, device=cuda_dev).to(torch.bfloat16)
+    big = torch.full((M, N + 64), 7.0, device=cuda_dev)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        gemm_nt(A, B, out=big[:, :N], dtype="bf16", stream=s)
+    s.synchronize()
+    assert _rel(big[:, :N], A.double() @ B.double().T) < 1e-4
+    assert torch.all(big[:, N:] == 7.0)
+
+
+def test_gemm_vs_reference_kernel(cuda_dev, oracle):
+    """Our bf16/tf32 GEMM against the reference's own fp32 tiled kernel."""
+    r = oracle.ref_lib()
+    if r is None:
+        pytest.skip("oracle/_ref not built (reference tree absent when building)")
+    from final_b200 import gemm_nt
+    M, N, K = 300, 3072, 2048
+    A = torch.randn(M, K, device=cuda_dev)
+    B = torch.randn(N, K, device=cuda_dev) * 0.02
+    Cref = torch.empty(M, N, device=cuda_dev)
+    assert r.ref_gemm_nt(C.c_void_p(Cref.data_ptr()), C.c_void_p(A.data_ptr()),
+                         C.c_void_p(B.data_ptr()), M, N, K, None) == 0
+    torch.cuda.synchronize()
+    exact = A.double() @ B.double().T
+    assert _rel(Cref, exact) < 1e-5  # the reference kernel itself is fp32-exact-ish
+    Cb = gemm_nt(A.to(torch.bfloat16), B.to(torch.bfloat16), dtype="bf16")
+    Ct = gemm_nt(A, B, dtype="tf32")
+    torch.cuda.synchronize()
+    assert _rel(Cb, Cref) < 1e-2
+    assert _rel(Ct, Cref) < 1e-2
+
+
+def test_gemm_invalid_args(cuda_dev):
+    from final_b200 import B2Error, gemm_nt
+    A = torch.zeros(4, 12, device=cuda_dev, dtype=torch.bfloat16)  # K=12: not a multiple of 8
+    B = torch.zeros(8, 12, device=cuda_dev, dtype=torch.bfloat16)
+    with pytest.raises(B2Error):
+        gemm_nt(A, B, dtype="bf16")
