@@ -15,6 +15,8 @@
 #pragma once
 #include "sm100_ptx.cuh"
 
+// Non-template kernels are `static`: each .cu that includes this header owns
+// its copy, so several translation units of the library can launch them.
 namespace b2 {
 
 constexpr int kRouteTB = 32;   // tokens per route / scatter block
@@ -29,7 +31,7 @@ constexpr int kMaxTopK = 8;
 // Thread (tg = tid%8, eg = tid/8) owns tokens 4tg..4tg+3 x experts 4eg..4eg+3.
 // gateT is the gate transposed to [H][32] (zero columns for e >= E).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(64)
+static __global__ void __launch_bounds__(64)
     route_kernel(const float *__restrict__ x, const float *__restrict__ gateT,
                  const float *__restrict__ bias, int T, int H, int E, int K,
                  float routed_scale, int *__restrict__ topk_idx,
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(64)
 // mtile_offsets = exclusive prefix of ceil(count/128) (+ sentinel);
 // block_base[b][e] = offsets[e] + sum_{b'<b} block_counts[b'][e].
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024)
+static __global__ void __launch_bounds__(1024)
     scan_kernel(const int *__restrict__ block_counts, int nb, int E, int tile_rows,
                 int *__restrict__ counts, int *__restrict__ offsets,
                 int *__restrict__ mtile_offsets, int *__restrict__ block_base) {
@@ -375,7 +377,7 @@ __global__ void pack_w2_single(const float *__restrict__ w2, int H, int I, int I
 }
 
 // gateT[h][e] = gate[e][h] for e < E, 0 otherwise (32 columns).
-__global__ void pack_gate_kernel(const float *__restrict__ gate, int E, int H,
+static __global__ void pack_gate_kernel(const float *__restrict__ gate, int E, int H,
                                  float *__restrict__ gateT) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)H * kMaxExperts) return;
@@ -383,7 +385,7 @@ __global__ void pack_gate_kernel(const float *__restrict__ gate, int E, int H,
   gateT[i] = e < E ? gate[(size_t)e * H + h] : 0.0f;
 }
 
-__global__ void f32_to_bf16_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out,
+static __global__ void f32_to_bf16_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out,
                                    size_t n) {
   size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const size_t stride = (size_t)gridDim.x * blockDim.x * 8;
