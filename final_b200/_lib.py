@@ -18,7 +18,7 @@ B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
 EXPORTED = (
     "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
     "b2_moe_get_status", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
-    "b2_kernel_launch_count", "b2_status_string", "b2_version",
+    "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
 )
 
 
@@ -67,13 +67,14 @@ def load(path: Path | None = None):
     lib.b2_moe_device_bytes.restype = sz
     lib.b2_gemm_nt.argtypes = [vp, vp, vp, i, i, i, i, i, vp, vp]
     lib.b2_convert_f32_to_bf16.argtypes = [vp, vp, sz, vp]
+    lib.b2_moe_route_noalloc.argtypes = [vp, vp, vp, i, i, i, i, C.c_float, vp, vp, vp, vp, vp, vp]
     lib.b2_kernel_launch_count.restype = C.c_uint64
     lib.b2_status_string.argtypes = [i]
     lib.b2_status_string.restype = C.c_char_p
     lib.b2_version.restype = C.c_char_p
     for name in ("b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
                  "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
-                 "b2_moe_profile_enable", "b2_moe_profile_read"):
+                 "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc"):
         getattr(lib, name).restype = i
     _lib = lib
     return lib

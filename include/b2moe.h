@@ -97,6 +97,26 @@ b2_status b2_moe_forward_ex(b2_moe *moe, const float *x, float *y,
                             int num_tokens, const b2_moe_trace *trace,
                             b2_stream stream);
 
+/* Routing step without any device allocation, for callers that may not call
+ * cudaMalloc after start-up (a server that plans all device memory up front,
+ * or a host whose allocator is owned elsewhere).  No counterpart in the
+ * reference: it is the route / scan / slot part of b2_moe_forward on caller
+ * buffers, with its scratch in a fixed 1 MiB __device__ array that every GPU
+ * loading this library holds until exit.
+ * x [T,H] f32, gate [E,H] f32, bias [E] f32 or NULL (device pointers);
+ * outputs topk_idx/topk_w/token_slot [T,K], counts/offsets [E].
+ * Limits: T <= 65536, H <= 4096 (multiple of 64), E <= 32, K <= 8; larger
+ * sizes return B2_ERR_CAPACITY.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must not be issued. */
+b2_status b2_moe_route_noalloc(const float *x, const float *gate,
+                               const float *bias, int num_tokens, int hidden,
+                               int num_experts, int top_k, float routed_scale,
+                               int32_t *topk_idx, float *topk_w,
+                               int32_t *counts, int32_t *offsets,
+                               int32_t *token_slot, b2_stream stream);
+
 /* Synchronises `stream`, returns the device status word (0 = ok) in
  * *device_status and clears it.  B2_ERR_DEVICE when it was non-zero. */
 b2_status b2_moe_get_status(b2_moe *moe, b2_stream stream, int *device_status);
