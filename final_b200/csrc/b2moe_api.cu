@@ -15,6 +15,7 @@
 
 #include "../../include/b2moe.h"
 #include "gemm_sm100.cuh"
+#include "host_tmap.h"
 #include "moe_kernels.cuh"
 
 using namespace b2;
@@ -38,43 +39,6 @@ std::atomic<uint64_t> g_launches{0};
     g_launches.fetch_add(1, std::memory_order_relaxed); \
     B2_CUDA(cudaGetLastError());                       \
   } while (0)
-
-// ------------------------------------------------------------ driver entry
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// 2-D K-major tile map with 128-byte swizzle: inner dim = k (elements),
-// outer = rows.  box = {128 bytes of k, box_rows}.
-bool make_tmap(CUtensorMap *m, const void *base, bool fp32, uint64_t inner, uint64_t rows,
-               uint64_t row_stride_bytes, uint32_t box_rows) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {row_stride_bytes};
-  const cuuint32_t box[2] = {fp32 ? 32u : 64u, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                   const_cast<void *>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
 
 struct DevInfo {
   int sms = 0;
@@ -342,9 +306,9 @@ extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int 
   const bool f = m->tf32;
 
   prof_mark(m, s);
-  route_kernel<<<nb, 64, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E, K,
-                                 m->d.routed_scale, m->topk_idx, m->topk_w, m->block_counts,
-                                 tr ? tr->logits : nullptr);
+  route_kernel<<<nb, kRouteThreads, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E,
+                                            K, m->d.routed_scale, m->topk_idx, m->topk_w,
+                                            m->block_counts, tr ? tr->logits : nullptr);
   B2_LAUNCHED();
   prof_mark(m, s);
   scan_kernel<<<1, 1024, 0, s>>>(m->block_counts, nb, E, kBM, m->counts, m->offsets, m->mtile,
@@ -352,12 +316,12 @@ extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int 
   B2_LAUNCHED();
   prof_mark(m, s);
   if (f)
-    scatter_kernel<float><<<nb, 32 * K, 0, s>>>(
+    scatter_kernel<float><<<nb, scatter_threads(K), 0, s>>>(
         x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
         reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token, m->sorted_w,
         m->status);
   else
-    scatter_kernel<__nv_bfloat16><<<nb, 32 * K, 0, s>>>(
+    scatter_kernel<__nv_bfloat16><<<nb, scatter_threads(K), 0, s>>>(
         x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
         reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot, m->sorted_token,
         m->sorted_w, m->status);

@@ -25,128 +25,182 @@ constexpr int kMaxExperts = 32;
 constexpr int kMaxTopK = 8;
 
 // ---------------------------------------------------------------------------
-// route_kernel: one block of 64 threads per 32 tokens.
+// route_kernel: one warp per 32 tokens.
 // logits[t,e] = fold_k fma(x[t,k], gate[e,k], acc) from 0.0f -- the order of
 // attn_matmul_tiled_kernel (src/layer.cu:70-130), so logits are bit-exact.
-// Thread (tg = tid%8, eg = tid/8) owns tokens 4tg..4tg+3 x experts 4eg..4eg+3.
-// gateT is the gate transposed to [H][32] (zero columns for e >= E).
+//
+// x and gateT (= gate^T, [H][32]) stream through a kRouteStages-deep cp.async
+// ring of 32-wide k-chunks: xs[t][k] holds 32 tokens x 32 k fp32 in rows
+// padded to 36 floats (the 4 rows one 128-bit load touches fall in distinct
+// bank groups, and every load offset is a compile-time constant); gs[k][e] is
+// the gate chunk.  A block is one warp, so the ring needs only warp-level
+// synchronisation.  Lane (tg = lane%4, eg = lane/4) owns tokens tg+4i (i<8)
+// x experts 4eg..4eg+3 (32 accumulators): per 4 k-steps, 12 128-bit shared
+// loads feed 128 FFMAs, each accumulator updated in strict k order.
 // ---------------------------------------------------------------------------
-static __global__ void __launch_bounds__(64)
+constexpr int kRouteStages = 4;
+constexpr int kRouteThreads = 32;
+constexpr int kRouteXRow = kRouteKC + 4;  // padded row (floats)
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+static __global__ void __launch_bounds__(kRouteThreads)
     route_kernel(const float *__restrict__ x, const float *__restrict__ gateT,
                  const float *__restrict__ bias, int T, int H, int E, int K,
                  float routed_scale, int *__restrict__ topk_idx,
                  float *__restrict__ topk_w, int *__restrict__ block_counts,
                  float *__restrict__ logits_out) {
-  __shared__ __align__(16) float xs[2][kRouteKC][kRouteTB + 4];
-  __shared__ __align__(16) float gs[2][kRouteKC][kMaxExperts];
+  __shared__ __align__(16) float xs[kRouteStages][kRouteTB * kRouteXRow];
+  __shared__ __align__(16) float gs[kRouteStages][kRouteKC * kMaxExperts];
   __shared__ float lg[kRouteTB][kMaxExperts + 1];
   __shared__ int hist[kMaxExperts];
 
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int wid = tid >> 5;
+  const int lane = threadIdx.x;
   const int t0 = blockIdx.x * kRouteTB;
-  const int tg = tid & 7, eg = tid >> 3;
   const int NC = H / kRouteKC;
-  const bool tok_ok = (t0 + lane) < T;
-  const float *xrow = x + (size_t)(t0 + lane) * H;
+  hist[lane] = 0;
 
-  if (tid < kMaxExperts) hist[tid] = 0;
-
-  // x chunk: lane = token, warp w loads k-quads 4w..4w+3 (float4 each)
-  float4 xr[4];
-  auto load_x = [&](int kc) {
+  // chunk kc -> stage st: 8 x 16 B of x and 8 x 16 B of the gate per lane;
+  // rows past T are zero-filled (src-size 0)
+  auto issue = [&](int kc, int st) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k0 = (wid * 4 + i) * 4;
-      xr[i] = tok_ok ? *reinterpret_cast<const float4 *>(xrow + kc * kRouteKC + k0)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int m = 0; m < 8; ++m) {
+      const int idx = lane + 32 * m;  // 0..255
+      const int row = idx >> 3, c = idx & 7;
+      const int t = t0 + row;
+      const bool ok = t < T;
+      const float *src = x + (size_t)(ok ? t : 0) * H + kc * kRouteKC + c * 4;
+      cp_async16(smem_u32(&xs[st][row * kRouteXRow + c * 4]), src, ok ? 16u : 0u);
     }
-  };
-  auto store_x = [&](int buf) {
+    const float *gsrc = gateT + (size_t)kc * kRouteKC * kMaxExperts;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k0 = (wid * 4 + i) * 4;
-      xs[buf][k0 + 0][lane] = xr[i].x;
-      xs[buf][k0 + 1][lane] = xr[i].y;
-      xs[buf][k0 + 2][lane] = xr[i].z;
-      xs[buf][k0 + 3][lane] = xr[i].w;
-    }
-  };
-  // gate chunk [KC][32] fp32 = 4 KB: 256 x 16 B, 4 per thread
-  auto load_g = [&](int kc, int buf) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int v = tid + i * 64;  // 16-byte vector index within the chunk
-      const float4 *src = reinterpret_cast<const float4 *>(gateT + (size_t)kc * kRouteKC * kMaxExperts) + v;
-      reinterpret_cast<float4 *>(&gs[buf][0][0])[v] = *src;
+    for (int m = 0; m < 8; ++m) {
+      const int idx = lane + 32 * m;  // 0..255
+      cp_async16(smem_u32(&gs[st][idx * 4]), gsrc + idx * 4, 16u);
     }
   };
 
-  float acc[4][4];
+  const int tg = lane & 3, eg = lane >> 2;
+  float acc[8][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
 
-  load_x(0);
-  store_x(0);
-  load_g(0, 0);
-  __syncthreads();
-  for (int kc = 0; kc < NC; ++kc) {
-    const int buf = kc & 1;
-    const bool more = kc + 1 < NC;
-    if (more) load_x(kc + 1);
-#pragma unroll 8
-    for (int k = 0; k < kRouteKC; ++k) {
-      const float4 xv = *reinterpret_cast<const float4 *>(&xs[buf][k][tg * 4]);
-      const float4 gv = *reinterpret_cast<const float4 *>(&gs[buf][k][eg * 4]);
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-      const float ga[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xa[i], ga[j], acc[i][j]);
-    }
-    if (more) {
-      store_x(buf ^ 1);
-      load_g(kc + 1, buf ^ 1);
-    }
-    __syncthreads();
+  for (int st = 0; st < kRouteStages - 1; ++st) {
+    if (st < NC) issue(st, st);
+    cp_async_commit();
   }
+  for (int kc = 0; kc < NC; ++kc) {
+    cp_async_wait<kRouteStages - 2>();
+    __syncwarp();
+    const int nk = kc + kRouteStages - 1;
+    if (nk < NC) issue(nk, nk % kRouteStages);
+    cp_async_commit();
+    const float *xb = xs[kc % kRouteStages] + tg * kRouteXRow;
+    const float *gb = gs[kc % kRouteStages] + eg * 4;
+#pragma unroll 2
+    for (int q = 0; q < kRouteKC / 4; ++q) {  // k-quad q: k = 4q .. 4q+3
+      float4 xv[8], gv[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i)
+        xv[i] = *reinterpret_cast<const float4 *>(xb + 4 * i * kRouteXRow + 4 * q);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) lg[tg * 4 + i][eg * 4 + j] = acc[i][j];
-  __syncthreads();
+      for (int j = 0; j < 4; ++j)
+        gv[j] = *reinterpret_cast<const float4 *>(gb + (4 * q + j) * kMaxExperts);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float ge[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xk = j == 0 ? xv[i].x : j == 1 ? xv[i].y : j == 2 ? xv[i].z : xv[i].w;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[i][e] = __fmaf_rn(xk, ge[e], acc[i][e]);
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with this stage before it is refilled
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) lg[tg + 4 * i][eg * 4 + e] = acc[i][e];
+  __syncwarp();
 
-  if (tid < kRouteTB) {
-    const int t = t0 + tid;
+  if (threadIdx.x < kRouteTB) {
+    const int tl = threadIdx.x;
+    const int t = t0 + tl;
     if (t < T) {
       if (logits_out)
-        for (int e = 0; e < E; ++e) logits_out[(size_t)t * E + e] = lg[tid][e];
-      float ms[kMaxTopK], mp[kMaxTopK];
+        for (int e = 0; e < E; ++e) logits_out[(size_t)t * E + e] = lg[tl][e];
+      float mp[kMaxTopK];
       int mi[kMaxTopK];
-#pragma unroll
-      for (int i = 0; i < kMaxTopK; ++i) {
-        ms[i] = -1e30f;
-        mp[i] = 0.0f;
-        mi[i] = -1;
-      }
-      for (int e = 0; e < E; ++e) {
-        const float prob = 1.0f / (1.0f + (float)exp(-(double)lg[tid][e]));
-        const float score = prob + (bias ? bias[e] : 0.0f);
-        if (score > ms[K - 1]) {
-          int pos = K - 1;
-          while (pos > 0 && score > ms[pos - 1]) {
-            ms[pos] = ms[pos - 1];
-            mp[pos] = mp[pos - 1];
-            mi[pos] = mi[pos - 1];
-            pos--;
+      if (K == 4) {
+        // the reference's 4-slot insertion (src/layer.cu:468-487) unrolled into
+        // registers: same strict '>' comparisons in the same order
+        float s0 = -1e30f, s1 = -1e30f, s2 = -1e30f, s3 = -1e30f;
+        float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+        int i0 = -1, i1 = -1, i2 = -1, i3 = -1;
+        for (int e = 0; e < E; ++e) {
+          const float prob = 1.0f / (1.0f + (float)exp(-(double)lg[tl][e]));
+          const float sc = prob + (bias ? bias[e] : 0.0f);
+          if (sc > s3) {
+            if (sc > s2) {
+              s3 = s2; p3 = p2; i3 = i2;
+              if (sc > s1) {
+                s2 = s1; p2 = p1; i2 = i1;
+                if (sc > s0) {
+                  s1 = s0; p1 = p0; i1 = i0;
+                  s0 = sc; p0 = prob; i0 = e;
+                } else {
+                  s1 = sc; p1 = prob; i1 = e;
+                }
+              } else {
+                s2 = sc; p2 = prob; i2 = e;
+              }
+            } else {
+              s3 = sc; p3 = prob; i3 = e;
+            }
           }
-          ms[pos] = score;
-          mp[pos] = prob;
-          mi[pos] = e;
+        }
+        mp[0] = p0; mp[1] = p1; mp[2] = p2; mp[3] = p3;
+        mi[0] = i0; mi[1] = i1; mi[2] = i2; mi[3] = i3;
+      } else {
+        float ms[kMaxTopK];
+#pragma unroll
+        for (int i = 0; i < kMaxTopK; ++i) {
+          ms[i] = -1e30f;
+          mp[i] = 0.0f;
+          mi[i] = -1;
+        }
+        for (int e = 0; e < E; ++e) {
+          const float prob = 1.0f / (1.0f + (float)exp(-(double)lg[tl][e]));
+          const float score = prob + (bias ? bias[e] : 0.0f);
+          if (score > ms[K - 1]) {
+            int pos = K - 1;
+            while (pos > 0 && score > ms[pos - 1]) {
+              ms[pos] = ms[pos - 1];
+              mp[pos] = mp[pos - 1];
+              mi[pos] = mi[pos - 1];
+              pos--;
+            }
+            ms[pos] = score;
+            mp[pos] = prob;
+            mi[pos] = e;
+          }
         }
       }
       float sum = 0.0f;
@@ -160,7 +214,7 @@ static __global__ void __launch_bounds__(64)
     }
   }
   __syncthreads();
-  if (tid < kMaxExperts) block_counts[(size_t)blockIdx.x * kMaxExperts + tid] = hist[tid];
+  if (threadIdx.x < kMaxExperts) block_counts[(size_t)blockIdx.x * kMaxExperts + threadIdx.x] = hist[threadIdx.x];
 }
 
 // ---------------------------------------------------------------------------
@@ -219,12 +273,15 @@ static __global__ void __launch_bounds__(1024)
 }
 
 // ---------------------------------------------------------------------------
-// scatter_kernel: block b handles tokens [32b, 32b+32) with 32*K threads,
+// scatter_kernel: block b handles tokens [16b, 16b+16) with 16*K threads
+// (rounded up to whole warps),
 // thread p owns pair (token 32b + p/K, rank p%K).  Its slot is
 //   block_base[b][e] + #{pairs p' < p in this block with the same expert}
 // which is the canonical token-major order of the CPU oracle.  Then the block
 // copies each token row once from fp32 x into its K slots as bf16 (or fp32).
 // ---------------------------------------------------------------------------
+__host__ __device__ constexpr int scatter_threads(int K) { return (kRouteTB * K + 31) / 32 * 32; }
+
 template <typename TOut>
 __global__ void __launch_bounds__(256)
     scatter_kernel(const float *__restrict__ x, const int *__restrict__ topk_idx,
@@ -266,26 +323,39 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
+  // row copy: 4 tokens per pass so each thread keeps 8 x 16 B loads in flight
   const int ntok = min(kRouteTB, T - blockIdx.x * kRouteTB);
-  for (int tl = 0; tl < ntok; ++tl) {
-    const float *src = x + (size_t)(blockIdx.x * kRouteTB + tl) * H;
+  const float *xblk = x + (size_t)blockIdx.x * kRouteTB * H;
+  for (int tl0 = 0; tl0 < ntok; tl0 += 4) {
     for (int c = p * 8; c < H; c += blockDim.x * 8) {
-      const float4 a = *reinterpret_cast<const float4 *>(src + c);
-      const float4 b = *reinterpret_cast<const float4 *>(src + c + 4);
-      if constexpr (sizeof(TOut) == 2) {
-        const uint4 v = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w),
-                                   pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
-        for (int k = 0; k < K; ++k) {
-          const int s = slot_s[tl * K + k];
-          if (s >= 0) *reinterpret_cast<uint4 *>(sorted_x + (size_t)s * H + c) = v;
+      float4 a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (tl0 + u < ntok) {
+          const float *src = xblk + (size_t)(tl0 + u) * H + c;
+          a[u] = *reinterpret_cast<const float4 *>(src);
+          b[u] = *reinterpret_cast<const float4 *>(src + 4);
         }
-      } else {
-        for (int k = 0; k < K; ++k) {
-          const int s = slot_s[tl * K + k];
-          if (s >= 0) {
-            float4 *d = reinterpret_cast<float4 *>(sorted_x + (size_t)s * H + c);
-            d[0] = a;
-            d[1] = b;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (tl0 + u >= ntok) break;
+        const int tl = tl0 + u;
+        if constexpr (sizeof(TOut) == 2) {
+          const uint4 v = make_uint4(pack_bf16(a[u].x, a[u].y), pack_bf16(a[u].z, a[u].w),
+                                     pack_bf16(b[u].x, b[u].y), pack_bf16(b[u].z, b[u].w));
+          for (int k = 0; k < K; ++k) {
+            const int s = slot_s[tl * K + k];
+            if (s >= 0) *reinterpret_cast<uint4 *>(sorted_x + (size_t)s * H + c) = v;
+          }
+        } else {
+          for (int k = 0; k < K; ++k) {
+            const int s = slot_s[tl * K + k];
+            if (s >= 0) {
+              float4 *d = reinterpret_cast<float4 *>(sorted_x + (size_t)s * H + c);
+              d[0] = a[u];
+              d[1] = b[u];
+            }
           }
         }
       }

@@ -109,13 +109,13 @@ extern "C" b2_status b2_moe_route_noalloc(const float *x, const float *gate, con
   pack_gate_kernel<<<(H * kMaxExperts + 255) / 256, 256, 0, s>>>(gate, E, H, gateT);
   if (cudaGetLastError() != cudaSuccess) return B2_ERR_CUDA;
   const int nb = (T + kRouteTB - 1) / kRouteTB;
-  route_kernel<<<nb, 64, 0, s>>>(x, gateT, bias, T, H, E, K, routed_scale, topk_idx, topk_w,
-                                 block_counts, nullptr);
+  route_kernel<<<nb, kRouteThreads, 0, s>>>(x, gateT, bias, T, H, E, K, routed_scale, topk_idx,
+                                            topk_w, block_counts, nullptr);
   if (cudaGetLastError() != cudaSuccess) return B2_ERR_CUDA;
   scan_kernel<<<1, 1024, 0, s>>>(block_counts, nb, E, 128, counts, offsets, tile_off, block_base);
   if (cudaGetLastError() != cudaSuccess) return B2_ERR_CUDA;
   // slot bookkeeping only: hidden 0 skips the row copy
-  scatter_kernel<__nv_bfloat16><<<nb, 32 * K, 0, s>>>(x, topk_idx, topk_w, block_base, T, 0, E, K,
+  scatter_kernel<__nv_bfloat16><<<nb, scatter_threads(K), 0, s>>>(x, topk_idx, topk_w, block_base, T, 0, E, K,
                                                       nullptr, token_slot, nullptr, nullptr,
                                                       nullptr);
   if (cudaGetLastError() != cudaSuccess) return B2_ERR_CUDA;
