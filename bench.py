@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-dense", action="store_true", help="skip the dense GEMM sweep")
+    p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
+                   help="expert placement when --gpus > 1")
     return p.parse_args()
 
 
@@ -149,15 +151,18 @@ def smi_index_for(dev_index: int):
 
 
 # ------------------------------------------------------------------ inputs
-def make_inputs(T, routing, dev, seed=SEED):
-    """x [T,H] fp32, gate [E,H] fp32, fp32 expert weights -- generated on the device."""
+def make_inputs(T, routing, dev, seed=SEED, token_seed=None):
+    """x [T,H] fp32, gate [E,H] fp32, fp32 expert weights -- generated on the
+    device.  Weights depend on `seed` only; tokens on `token_seed` (default
+    `seed`), so expert-parallel ranks share one layer but hold different tokens."""
     import torch
+    gx = torch.Generator(device=dev).manual_seed(seed if token_seed is None else token_seed)
     g = torch.Generator(device=dev).manual_seed(seed)
-    x = torch.randn(T, H, device=dev, generator=g)
+    x = torch.randn(T, H, device=dev, generator=gx)
     if routing == "zipf":
         p = torch.arange(1, E + 1, dtype=torch.float64, device=dev) ** (-ZIPF_S)
         p = p / p.sum()
-        u = torch.rand(T, E, device=dev, generator=g, dtype=torch.float64).clamp_min(1e-300)
+        u = torch.rand(T, E, device=dev, generator=gx, dtype=torch.float64).clamp_min(1e-300)
         L = (p.log()[None, :] - torch.log(-torch.log(u))).float()
         gate = torch.zeros(E, H, device=dev)
         gate[torch.arange(E), torch.arange(E)] = 1.0
@@ -183,8 +188,13 @@ def run_ours(args, rank, world, dev):
     from final_b200 import SparseMoeBlock, launch_count
 
     T = args.tokens
-    x, gate, bias, w1, w2, w3 = make_inputs(T, args.routing, dev, SEED + rank)
-    layer = SparseMoeBlock(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype)
+    x, gate, bias, w1, w2, w3 = make_inputs(T, args.routing, dev, SEED, SEED + 1000 * (rank + 1))
+    if world > 1:
+        from final_b200.ep import ExpertParallelMoE
+        layer = ExpertParallelMoE(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype,
+                                  mode=args.ep_mode, timeout_s=120.0)
+    else:
+        layer = SparseMoeBlock(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype)
     w_host = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # fp32 weights for the CPU baseline sample (same workload)
@@ -194,11 +204,22 @@ def run_ours(args, rank, world, dev):
     del w1, w2, w3
     torch.cuda.empty_cache()
     y = torch.empty(T, H, device=dev)
-    counts_probe = layer.forward_traced(x)["counts"].cpu().tolist()
+    if world > 1:
+        layer.forward_gpu(x, y, T)
+        torch.cuda.synchronize()
+        plan = layer.last_plan()
+        rows = torch.tensor([plan["recv_rows"]], device=dev)
+        all_rows = [torch.zeros_like(rows) for _ in range(world)]
+        dist.all_gather(all_rows, rows)
+        counts_probe = [int(r.item()) for r in all_rows]   # rows each rank computes
+    else:
+        counts_probe = layer.forward_traced(x)["counts"].cpu().tolist()
 
     stream = torch.cuda.current_stream()
+    fwd = (lambda xi, yi: layer.forward_gpu(xi, yi, T, stream)) if world > 1 else \
+        (lambda xi, yi: layer.forward_gpu(xi, yi, 1, T, H, stream))
     for _ in range(args.warmup):
-        layer.forward_gpu(x, y, 1, T, H, stream)
+        fwd(x, y)
     torch.cuda.synchronize()
     st = layer.device_status()
     if st != 0:
@@ -214,7 +235,7 @@ def run_ours(args, rank, world, dev):
     n0 = launch_count()
     ev0.record(stream)
     for _ in range(args.steps):
-        layer.forward_gpu(x, y, 1, T, H, stream)
+        fwd(x, y)
     ev1.record(stream)
     torch.cuda.synchronize()
     n1 = launch_count()
@@ -258,7 +279,7 @@ def run_ours(args, rank, world, dev):
                 stream.wait_event(e_in)
                 if done_o[b] is not None:
                     stream.wait_event(done_o[b])
-                layer.forward_gpu(xd[b], yd[b], 1, T, H, stream)
+                fwd(xd[b], yd[b])
                 e_c = ev(); e_c.record(stream); done_c[b] = e_c
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(e_c)
@@ -318,10 +339,12 @@ def run_ours(args, rank, world, dev):
                    "hidden": H, "experts": E, "top_k": K, "inter": I,
                    "routing": ("zipf(1.1) injected logits" if args.routing == "zipf"
                                else "x.gate N(0,1)xN(0,0.02), bias N(0,0.02)"),
-                   "expert_load_max_min": [max(counts_probe), min(counts_probe)],
+                   ("rows_per_rank" if world > 1 else "expert_load_max_min"):
+                       counts_probe if world > 1 else [max(counts_probe), min(counts_probe)],
                    "weights": f"{args.dtype} packed from fp32 N(0,0.02)",
                    "l2": "inputs larger than L2: x 134 MB fp32, expert weights 705 MB bf16",
-                   "parallelism": "replicas" if world > 1 else "single"},
+                   "parallelism": (f"expert-parallel ep{world} ({args.ep_mode}), NCCL dispatch/combine"
+                                   if world > 1 else "single")},
         "layer_tflops": flop * args.steps * world / (ms / 1e3) / 1e12 / world,
         "grouped_gemm_tflops": gemm_flop / ((w13_ms + w2_ms) / 1e3) / 1e12,
         "frac_of_bf16_peak_layer": flop / (ms / args.steps / 1e3) / 1e12 / pk["bf16"],

@@ -11,7 +11,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2moe.so"
 
-B2_OK, B2_ERR_INVALID, B2_ERR_CUDA, B2_ERR_CAPACITY, B2_ERR_DEVICE, B2_ERR_NO_DEVICE = range(6)
+B2_OK, B2_ERR_INVALID, B2_ERR_CUDA, B2_ERR_CAPACITY, B2_ERR_DEVICE, B2_ERR_NO_DEVICE, B2_ERR_COMM = range(7)
 B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
 
 # Every symbol include/b2moe.h declares (checked by tests/test_abi.py).
@@ -19,7 +19,14 @@ EXPORTED = (
     "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
     "b2_moe_get_status", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
     "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
+    # include/b2moe_ep.h
+    "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
+    "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy",
 )
+
+EP_MAX_WORLD = 64
+EP_MAX_SEGMENTS = 256
+B2_EP_OWNER, B2_EP_BALANCED = 0, 1
 
 
 class B2Error(RuntimeError):
@@ -39,6 +46,23 @@ class MoeTrace(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in (
         "logits", "topk_idx", "topk_w", "counts", "offsets", "mtile_offsets",
         "token_slot", "sorted_token", "sorted_w")]
+
+
+class EpPlan(C.Structure):
+    _fields_ = [("send_off", C.c_int64 * EP_MAX_WORLD), ("send_cnt", C.c_int64 * EP_MAX_WORLD),
+                ("recv_off", C.c_int64 * EP_MAX_WORLD), ("recv_cnt", C.c_int64 * EP_MAX_WORLD),
+                ("recv_rows", C.c_int64), ("num_segments", C.c_int32),
+                ("seg_off", C.c_int32 * EP_MAX_SEGMENTS), ("seg_cnt", C.c_int32 * EP_MAX_SEGMENTS),
+                ("seg_expert", C.c_int32 * EP_MAX_SEGMENTS),
+                ("seg_source", C.c_int32 * EP_MAX_SEGMENTS)]
+
+    def to_dict(self, world: int) -> dict:
+        n = self.num_segments
+        return {"send_off": list(self.send_off[:world]), "send_cnt": list(self.send_cnt[:world]),
+                "recv_off": list(self.recv_off[:world]), "recv_cnt": list(self.recv_cnt[:world]),
+                "recv_rows": int(self.recv_rows), "seg_off": list(self.seg_off[:n]),
+                "seg_cnt": list(self.seg_cnt[:n]), "seg_expert": list(self.seg_expert[:n]),
+                "seg_source": list(self.seg_source[:n])}
 
 
 _lib = None
@@ -68,13 +92,25 @@ def load(path: Path | None = None):
     lib.b2_gemm_nt.argtypes = [vp, vp, vp, i, i, i, i, i, vp, vp]
     lib.b2_convert_f32_to_bf16.argtypes = [vp, vp, sz, vp]
     lib.b2_moe_route_noalloc.argtypes = [vp, vp, vp, i, i, i, i, C.c_float, vp, vp, vp, vp, vp, vp]
+    lib.b2_ep_plan_compute.argtypes = [i, i, i, i, vp, C.POINTER(EpPlan)]
+    lib.b2_ep_unique_id.argtypes = [vp]
+    lib.b2_ep_create.argtypes = [C.POINTER(MoeDesc), i, i, vp, i, vp, vp, vp, vp, vp, i, vp,
+                                 C.POINTER(vp)]
+    lib.b2_ep_forward.argtypes = [vp, vp, vp, i, vp]
+    lib.b2_ep_set_timeout.argtypes = [vp, C.c_double]
+    lib.b2_ep_last_plan.argtypes = [vp, C.POINTER(EpPlan)]
+    lib.b2_ep_layer.argtypes = [vp]
+    lib.b2_ep_layer.restype = vp
+    lib.b2_ep_destroy.argtypes = [vp]
     lib.b2_kernel_launch_count.restype = C.c_uint64
     lib.b2_status_string.argtypes = [i]
     lib.b2_status_string.restype = C.c_char_p
     lib.b2_version.restype = C.c_char_p
     for name in ("b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
                  "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
-                 "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc"):
+                 "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc",
+                 "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
+                 "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy"):
         getattr(lib, name).restype = i
     _lib = lib
     return lib

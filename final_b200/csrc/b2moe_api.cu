@@ -1,4 +1,4 @@
-// b2moe_api.cu -- implementation of the C ABI in include/b2moe.h.
+// b2moe_api.cu -- implementation of the single-GPU C ABI in include/b2moe.h.
 //
 // Owns the packed weights, the scratch buffers and the TMA descriptors of an
 // MoE layer object, and launches the kernel pipeline of moe_kernels.cuh and
@@ -10,95 +10,18 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
-#include <mutex>
 #include <vector>
 
-#include "../../include/b2moe.h"
-#include "gemm_sm100.cuh"
-#include "host_tmap.h"
-#include "moe_kernels.cuh"
+#include "moe_internal.h"
 
 using namespace b2;
 
-namespace {
+namespace b2 {
 
-std::atomic<uint64_t> g_launches{0};
-
-#define B2_CUDA(call)                                                                  \
-  do {                                                                                 \
-    cudaError_t e_ = (call);                                                           \
-    if (e_ != cudaSuccess) {                                                           \
-      fprintf(stderr, "[b2moe] %s failed at %s:%d: %s\n", #call, __FILE__, __LINE__,   \
-              cudaGetErrorString(e_));                                                 \
-      return B2_ERR_CUDA;                                                              \
-    }                                                                                  \
-  } while (0)
-
-#define B2_LAUNCHED()                                  \
-  do {                                                 \
-    g_launches.fetch_add(1, std::memory_order_relaxed); \
-    B2_CUDA(cudaGetLastError());                       \
-  } while (0)
-
-struct DevInfo {
-  int sms = 0;
-  int cc_major = 0;
-};
-
-bool dev_info(DevInfo *d) {
-  int dev;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  if (cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return false;
-  if (cudaDeviceGetAttribute(&d->cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-    return false;
-  return true;
+std::atomic<uint64_t> &launch_counter() {
+  static std::atomic<uint64_t> n{0};
+  return n;
 }
-
-template <int EPI, bool TF32, typename TOut>
-b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
-                      int grid, cudaStream_t s) {
-  auto kern = gemm_sm100_kernel<EPI, TF32, TOut>;
-  const size_t smem = gemm_smem_bytes();
-  // per-device attribute; cheap enough to set on every launch
-  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  if (grid <= 0) return B2_OK;
-  kern<<<grid, kGemmThreads, smem, s>>>(ta, tb, args);
-  B2_LAUNCHED();
-  return B2_OK;
-}
-
-}  // namespace
-
-// ---------------------------------------------------------------- MoE object
-struct b2_moe {
-  b2_moe_desc d;
-  int device = 0;
-  int Ip = 0;  // inter padded to 128
-  int sms = 0;
-  bool tf32 = false;
-  size_t bytes = 0;
-  // weights
-  float *gateT = nullptr;
-  float *bias = nullptr;
-  void *w13 = nullptr;  // [E][2Ip][H]
-  void *w2 = nullptr;   // [E][H][Ip]
-  // scratch
-  int *topk_idx = nullptr, *block_counts = nullptr, *block_base = nullptr;
-  int *counts = nullptr, *offsets = nullptr, *mtile = nullptr;
-  int *token_slot = nullptr, *sorted_token = nullptr;
-  float *topk_w = nullptr, *sorted_w = nullptr;
-  void *sorted_x = nullptr, *inter = nullptr, *sout = nullptr;
-  int *status = nullptr;
-  CUtensorMap tm_x, tm_w13, tm_inter, tm_w2;
-  std::vector<void *> allocs;
-  // stage profiling
-  bool profile = false;
-  std::vector<cudaEvent_t> ev_pool;   // free events
-  std::vector<cudaEvent_t> ev_rec;    // kStageEvents per recorded forward
-};
-
-static constexpr int kStageEvents = 7;
 
 static cudaEvent_t prof_event(b2_moe *m) {
   if (!m->ev_pool.empty()) {
@@ -111,14 +34,14 @@ static cudaEvent_t prof_event(b2_moe *m) {
   return e;
 }
 
-static void prof_mark(b2_moe *m, cudaStream_t s) {
+void prof_mark(b2_moe *m, cudaStream_t s) {
   if (!m->profile) return;
   cudaEvent_t e = prof_event(m);
   cudaEventRecord(e, s);
   m->ev_rec.push_back(e);
 }
 
-static b2_status moe_alloc(b2_moe *m, void **p, size_t bytes) {
+b2_status moe_alloc(b2_moe *m, void **p, size_t bytes) {
   if (bytes == 0) bytes = 16;
   B2_CUDA(cudaMalloc(p, bytes));
   m->allocs.push_back(*p);
@@ -135,6 +58,8 @@ static void moe_free_all(b2_moe *m) {
   m->ev_rec.clear();
 }
 
+}  // namespace b2
+
 extern "C" b2_status b2_moe_destroy(b2_moe *moe) {
   if (!moe) return B2_OK;
   int prev = 0;
@@ -146,48 +71,52 @@ extern "C" b2_status b2_moe_destroy(b2_moe *moe) {
   return B2_OK;
 }
 
-#define B2_TRY(x)                      \
-  do {                                 \
-    b2_status s_ = (x);                \
-    if (s_ != B2_OK) {                 \
-      b2_moe_destroy(m);               \
-      return s_;                       \
-    }                                  \
-  } while (0)
+namespace b2 {
 
-extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *w1,
-                                   const float *const *w2, const float *const *w3,
-                                   const float *gate, const float *bias, int weights_on_host,
-                                   b2_stream stream_, b2_moe **out) {
-  if (!desc || !w1 || !w2 || !w3 || !gate || !out) return B2_ERR_INVALID;
+b2_status moe_create_impl(const b2_moe_desc *desc, int n_wexp, const float *const *w1,
+                          const float *const *w2, const float *const *w3, const float *gate,
+                          const float *bias, int weights_on_host, cudaStream_t stream,
+                          bool local_gemm_buffers, b2_moe **out) {
+  if (!desc || !out || !gate || (n_wexp > 0 && (!w1 || !w2 || !w3))) return B2_ERR_INVALID;
   *out = nullptr;
   const b2_moe_desc &d = *desc;
   if (d.hidden <= 0 || d.hidden % 64 != 0 || d.inter <= 0 || d.inter % 16 != 0 ||
       d.num_experts < 1 || d.num_experts > kMaxExperts || d.top_k < 1 || d.top_k > kMaxTopK ||
-      d.top_k > d.num_experts || d.max_tokens < 1 || (d.dtype != B2_BF16 && d.dtype != B2_TF32))
+      d.top_k > d.num_experts || d.max_tokens < 1 || (d.dtype != B2_BF16 && d.dtype != B2_TF32) ||
+      n_wexp < 0 || n_wexp > kMaxGroups)
     return B2_ERR_INVALID;
   if (d.use_bias && !bias) return B2_ERR_INVALID;
   DevInfo di;
   if (!dev_info(&di)) return B2_ERR_NO_DEVICE;
   if (di.cc_major != 10) return B2_ERR_NO_DEVICE;
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
 
   b2_moe *m = new b2_moe();
   m->d = d;
+  m->n_wexp = n_wexp;
   cudaGetDevice(&m->device);
   m->sms = di.sms;
   m->tf32 = d.dtype == B2_TF32;
   const int E = d.num_experts, H = d.hidden, I = d.inter, K = d.top_k;
+  const int W = n_wexp;
   m->Ip = (I + 127) / 128 * 128;
   const int Ip = m->Ip;
   const size_t es = m->tf32 ? 4 : 2;
   const size_t T = (size_t)d.max_tokens, R = T * K;
   const size_t nb = (T + kRouteTB - 1) / kRouteTB;
 
+  auto bail = [&](b2_status s) {
+    b2_moe_destroy(m);
+    return s;
+  };
+#define B2_TRY(x)                     \
+  do {                                \
+    b2_status s_ = (x);               \
+    if (s_ != B2_OK) return bail(s_); \
+  } while (0)
   B2_TRY(moe_alloc(m, (void **)&m->gateT, sizeof(float) * H * kMaxExperts));
   B2_TRY(moe_alloc(m, (void **)&m->bias, sizeof(float) * kMaxExperts));
-  B2_TRY(moe_alloc(m, &m->w13, es * (size_t)E * 2 * Ip * H));
-  B2_TRY(moe_alloc(m, &m->w2, es * (size_t)E * H * Ip));
+  B2_TRY(moe_alloc(m, &m->w13, es * (size_t)std::max(W, 1) * 2 * Ip * H));
+  B2_TRY(moe_alloc(m, &m->w2, es * (size_t)std::max(W, 1) * H * Ip));
   B2_TRY(moe_alloc(m, (void **)&m->topk_idx, sizeof(int) * R));
   B2_TRY(moe_alloc(m, (void **)&m->topk_w, sizeof(float) * R));
   B2_TRY(moe_alloc(m, (void **)&m->block_counts, sizeof(int) * nb * kMaxExperts));
@@ -199,15 +128,13 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
   B2_TRY(moe_alloc(m, (void **)&m->sorted_token, sizeof(int) * R));
   B2_TRY(moe_alloc(m, (void **)&m->sorted_w, sizeof(float) * R));
   B2_TRY(moe_alloc(m, &m->sorted_x, es * R * H));
-  B2_TRY(moe_alloc(m, &m->inter, es * R * Ip));
+  if (local_gemm_buffers) B2_TRY(moe_alloc(m, &m->inter, es * R * Ip));
   B2_TRY(moe_alloc(m, &m->sout, es * R * H));
   B2_TRY(moe_alloc(m, (void **)&m->status, sizeof(int)));
   if (cudaMemsetAsync(m->status, 0, sizeof(int), stream) != cudaSuccess ||
       cudaMemsetAsync(m->bias, 0, sizeof(float) * kMaxExperts, stream) != cudaSuccess ||
-      cudaMemsetAsync(m->inter, 0, es * R * Ip, stream) != cudaSuccess) {
-    b2_moe_destroy(m);
-    return B2_ERR_CUDA;
-  }
+      (m->inter && cudaMemsetAsync(m->inter, 0, es * R * Ip, stream) != cudaSuccess))
+    return bail(B2_ERR_CUDA);
 
   // ---- weights: stage host matrices through one expert-sized device buffer
   float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr, *stg = nullptr;
@@ -216,8 +143,7 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
     if (st3) cudaFree(st3);
     if (st2) cudaFree(st2);
     if (stg) cudaFree(stg);
-    b2_moe_destroy(m);
-    return s;
+    return bail(s);
   };
   const size_t mat = (size_t)I * H;
   if (weights_on_host) {
@@ -226,7 +152,7 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
         cudaMalloc(&stg, sizeof(float) * E * H) != cudaSuccess)
       return fail(B2_ERR_CUDA);
   }
-  for (int e = 0; e < E; ++e) {
+  for (int e = 0; e < W; ++e) {
     const float *p1 = w1[e], *p3 = w3[e], *p2 = w2[e];
     if (!p1 || !p2 || !p3) return fail(B2_ERR_INVALID);
     if (weights_on_host) {
@@ -250,7 +176,7 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
       pack_w2_single<__nv_bfloat16><<<H, 256, 0, stream>>>(p2, H, I, Ip, o2);
     }
     if (cudaGetLastError() != cudaSuccess) return fail(B2_ERR_CUDA);
-    g_launches.fetch_add(2, std::memory_order_relaxed);
+    launch_counter().fetch_add(2, std::memory_order_relaxed);
     if (weights_on_host && cudaStreamSynchronize(stream) != cudaSuccess)
       return fail(B2_ERR_CUDA);  // staging buffers are reused by the next expert
   }
@@ -263,7 +189,7 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
   }
   pack_gate_kernel<<<(H * kMaxExperts + 255) / 256, 256, 0, stream>>>(gsrc, E, H, m->gateT);
   if (cudaGetLastError() != cudaSuccess) return fail(B2_ERR_CUDA);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   if (d.use_bias &&
       cudaMemcpyAsync(m->bias, bias, sizeof(float) * E,
                       weights_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
@@ -278,15 +204,110 @@ extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *
 
   // ---- TMA descriptors (buffers are fixed for the object's lifetime)
   const bool f = m->tf32;
+  const int Wm = std::max(W, 1);
   if (!make_tmap(&m->tm_x, m->sorted_x, f, H, R, (uint64_t)H * es, kBM) ||
-      !make_tmap(&m->tm_w13, m->w13, f, H, (uint64_t)E * 2 * Ip, (uint64_t)H * es, kBN) ||
-      !make_tmap(&m->tm_inter, m->inter, f, Ip, R, (uint64_t)Ip * es, kBM) ||
-      !make_tmap(&m->tm_w2, m->w2, f, Ip, (uint64_t)E * H, (uint64_t)Ip * es, kBN)) {
-    b2_moe_destroy(m);
-    return B2_ERR_CUDA;
-  }
+      !make_tmap(&m->tm_w13, m->w13, f, H, (uint64_t)Wm * 2 * Ip, (uint64_t)H * es, kBN) ||
+      (m->inter && !make_tmap(&m->tm_inter, m->inter, f, Ip, R, (uint64_t)Ip * es, kBM)) ||
+      !make_tmap(&m->tm_w2, m->w2, f, Ip, (uint64_t)Wm * H, (uint64_t)Ip * es, kBN))
+    return bail(B2_ERR_CUDA);
+#undef B2_TRY
   *out = m;
   return B2_OK;
+}
+
+b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *tr,
+                          cudaStream_t s) {
+  const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden;
+  const int nb = (T + kRouteTB - 1) / kRouteTB;
+  prof_mark(m, s);
+  route_kernel<<<nb, kRouteThreads, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E,
+                                            K, m->d.routed_scale, m->topk_idx, m->topk_w,
+                                            m->block_counts, tr ? tr->logits : nullptr);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+  scan_kernel<<<1, 1024, 0, s>>>(m->block_counts, nb, E, kBM, m->counts, m->offsets, m->mtile,
+                                 m->block_base);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+  if (m->tf32)
+    scatter_kernel<float><<<nb, scatter_threads(K), 0, s>>>(
+        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
+        reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token, m->sorted_w,
+        m->status);
+  else
+    scatter_kernel<__nv_bfloat16><<<nb, scatter_threads(K), 0, s>>>(
+        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
+        reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot, m->sorted_token,
+        m->sorted_w, m->status);
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
+b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap &tm_a2,
+                         void *inter, void *out, const GemmSched &sc, cudaStream_t s,
+                         bool stage_marks) {
+  const int H = m->d.hidden, Ip = m->Ip;
+  const bool f = m->tf32;
+  GemmArgs a1{};
+  a1.counts = sc.counts;
+  a1.offsets = sc.offsets;
+  a1.mtile_offsets = sc.mtile_offsets;
+  a1.group_b = sc.group_b;
+  a1.num_groups = sc.num_groups;
+  a1.b_rows_per_group = 2 * Ip;
+  a1.N = Ip;
+  a1.num_n_tiles = Ip / 128;
+  a1.num_k_blocks = f ? H / 32 : H / 64;
+  a1.out = inter;
+  a1.ldo = Ip;
+  a1.status = m->status;
+  const int grid1 = (int)std::min<long long>(m->sms, sc.mtiles_upper_bound * a1.num_n_tiles);
+  if (stage_marks) prof_mark(m, s);
+  if (f)
+    B2_RETURN_IF((launch_gemm<kEpiSwiGLU, true, float>(tm_a1, m->tm_w13, a1, grid1, s)));
+  else
+    B2_RETURN_IF((launch_gemm<kEpiSwiGLU, false, __nv_bfloat16>(tm_a1, m->tm_w13, a1, grid1, s)));
+
+  GemmArgs a2 = a1;
+  a2.b_rows_per_group = H;
+  a2.N = H;
+  a2.num_n_tiles = (H + kBN - 1) / kBN;
+  a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
+  a2.out = out;
+  a2.ldo = H;
+  const int grid2 = (int)std::min<long long>(m->sms, sc.mtiles_upper_bound * a2.num_n_tiles);
+  if (stage_marks) prof_mark(m, s);
+  if (f)
+    B2_RETURN_IF((launch_gemm<kEpiStore, true, float>(tm_a2, m->tm_w2, a2, grid2, s)));
+  else
+    B2_RETURN_IF((launch_gemm<kEpiStore, false, __nv_bfloat16>(tm_a2, m->tm_w2, a2, grid2, s)));
+  return B2_OK;
+}
+
+b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s) {
+  const int K = m->d.top_k, H = m->d.hidden;
+  prof_mark(m, s);
+  if (m->tf32)
+    combine_kernel<float><<<T, 256, 0, s>>>(reinterpret_cast<const float *>(m->sout),
+                                            m->token_slot, m->topk_w, T, H, K, y);
+  else
+    combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(m->sout), m->token_slot, m->topk_w, T, H, K, y);
+  B2_LAUNCHED();
+  prof_mark(m, s);
+  return B2_OK;
+}
+
+}  // namespace b2
+
+// ---------------------------------------------------------------- C ABI
+extern "C" b2_status b2_moe_create(const b2_moe_desc *desc, const float *const *w1,
+                                   const float *const *w2, const float *const *w3,
+                                   const float *gate, const float *bias, int weights_on_host,
+                                   b2_stream stream, b2_moe **out) {
+  if (!desc) return B2_ERR_INVALID;
+  return moe_create_impl(desc, desc->num_experts, w1, w2, w3, gate, bias, weights_on_host,
+                         reinterpret_cast<cudaStream_t>(stream), true, out);
 }
 
 static b2_status copy_trace(void *dst, const void *src, size_t bytes, cudaStream_t s) {
@@ -298,96 +319,33 @@ static b2_status copy_trace(void *dst, const void *src, size_t bytes, cudaStream
 extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int T,
                                        const b2_moe_trace *tr, b2_stream stream_) {
   if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (m->n_wexp != m->d.num_experts || !m->inter) return B2_ERR_INVALID;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   if (T == 0) return B2_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
-  const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden, Ip = m->Ip;
-  const int nb = (T + kRouteTB - 1) / kRouteTB;
-  const bool f = m->tf32;
+  const int E = m->d.num_experts, K = m->d.top_k;
 
-  prof_mark(m, s);
-  route_kernel<<<nb, kRouteThreads, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E,
-                                            K, m->d.routed_scale, m->topk_idx, m->topk_w,
-                                            m->block_counts, tr ? tr->logits : nullptr);
-  B2_LAUNCHED();
-  prof_mark(m, s);
-  scan_kernel<<<1, 1024, 0, s>>>(m->block_counts, nb, E, kBM, m->counts, m->offsets, m->mtile,
-                                 m->block_base);
-  B2_LAUNCHED();
-  prof_mark(m, s);
-  if (f)
-    scatter_kernel<float><<<nb, scatter_threads(K), 0, s>>>(
-        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
-        reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token, m->sorted_w,
-        m->status);
-  else
-    scatter_kernel<__nv_bfloat16><<<nb, scatter_threads(K), 0, s>>>(
-        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
-        reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot, m->sorted_token,
-        m->sorted_w, m->status);
-  B2_LAUNCHED();
-
-  const long long R = (long long)T * K;
-  const int mt_ub = (int)((R + kBM - 1) / kBM) + E;  // each expert adds <= 1 partial tile
-
-  GemmArgs a1{};
-  a1.counts = m->counts;
-  a1.offsets = m->offsets;
-  a1.mtile_offsets = m->mtile;
-  a1.num_groups = E;
-  a1.b_rows_per_group = 2 * Ip;
-  a1.N = Ip;
-  a1.num_n_tiles = Ip / 128;
-  a1.num_k_blocks = f ? H / 32 : H / 64;
-  a1.out = m->inter;
-  a1.ldo = Ip;
-  a1.status = m->status;
-  const int grid1 = (int)std::min<long long>(m->sms, (long long)mt_ub * a1.num_n_tiles);
-  b2_status st;
-  prof_mark(m, s);
-  if (f)
-    st = launch_gemm<kEpiSwiGLU, true, float>(m->tm_x, m->tm_w13, a1, grid1, s);
-  else
-    st = launch_gemm<kEpiSwiGLU, false, __nv_bfloat16>(m->tm_x, m->tm_w13, a1, grid1, s);
-  if (st != B2_OK) return st;
-
-  GemmArgs a2 = a1;
-  a2.b_rows_per_group = H;
-  a2.N = H;
-  a2.num_n_tiles = (H + kBN - 1) / kBN;
-  a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
-  a2.out = m->sout;
-  a2.ldo = H;
-  const int grid2 = (int)std::min<long long>(m->sms, (long long)mt_ub * a2.num_n_tiles);
-  prof_mark(m, s);
-  if (f)
-    st = launch_gemm<kEpiStore, true, float>(m->tm_inter, m->tm_w2, a2, grid2, s);
-  else
-    st = launch_gemm<kEpiStore, false, __nv_bfloat16>(m->tm_inter, m->tm_w2, a2, grid2, s);
-  if (st != B2_OK) return st;
-
-  prof_mark(m, s);
-  if (f)
-    combine_kernel<float><<<T, 256, 0, s>>>(reinterpret_cast<const float *>(m->sout),
-                                            m->token_slot, m->topk_w, T, H, K, y);
-  else
-    combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(m->sout), m->token_slot, m->topk_w, T, H, K, y);
-  B2_LAUNCHED();
-  prof_mark(m, s);
+  B2_RETURN_IF(moe_route_stage(m, x, T, tr, s));
+  GemmSched sc;
+  sc.counts = m->counts;
+  sc.offsets = m->offsets;
+  sc.mtile_offsets = m->mtile;
+  sc.group_b = nullptr;
+  sc.num_groups = E;
+  sc.mtiles_upper_bound = ((long long)T * K + kBM - 1) / kBM + E;  // <= 1 partial tile per expert
+  B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, m->tm_inter, m->inter, m->sout, sc, s));
+  B2_RETURN_IF(moe_combine_stage(m, y, T, s));
 
   if (tr) {
     const size_t tk = (size_t)T * K;
-    b2_status c = B2_OK;
-    if (c == B2_OK) c = copy_trace(tr->topk_idx, m->topk_idx, tk * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->topk_w, m->topk_w, tk * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->counts, m->counts, (size_t)E * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->offsets, m->offsets, (size_t)E * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->mtile_offsets, m->mtile, (size_t)(E + 1) * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->token_slot, m->token_slot, tk * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->sorted_token, m->sorted_token, tk * 4, s);
-    if (c == B2_OK) c = copy_trace(tr->sorted_w, m->sorted_w, tk * 4, s);
-    if (c != B2_OK) return c;
+    B2_RETURN_IF(copy_trace(tr->topk_idx, m->topk_idx, tk * 4, s));
+    B2_RETURN_IF(copy_trace(tr->topk_w, m->topk_w, tk * 4, s));
+    B2_RETURN_IF(copy_trace(tr->counts, m->counts, (size_t)E * 4, s));
+    B2_RETURN_IF(copy_trace(tr->offsets, m->offsets, (size_t)E * 4, s));
+    B2_RETURN_IF(copy_trace(tr->mtile_offsets, m->mtile, (size_t)(E + 1) * 4, s));
+    B2_RETURN_IF(copy_trace(tr->token_slot, m->token_slot, tk * 4, s));
+    B2_RETURN_IF(copy_trace(tr->sorted_token, m->sorted_token, tk * 4, s));
+    B2_RETURN_IF(copy_trace(tr->sorted_w, m->sorted_w, tk * 4, s));
   }
   return B2_OK;
 }
@@ -471,7 +429,8 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
 extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,
                                             b2_stream stream_) {
   if (n == 0) return B2_OK;
-  if (!in || !out || (reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+  if (!in || !out || (reinterpret_cast<uintptr_t>(in) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
     return B2_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   const size_t blocks = std::min<size_t>((n / 8 + 255) / 256 + 1, 148 * 16);
@@ -480,7 +439,7 @@ extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n
   return B2_OK;
 }
 
-extern "C" uint64_t b2_kernel_launch_count(void) { return g_launches.load(); }
+extern "C" uint64_t b2_kernel_launch_count(void) { return launch_counter().load(); }
 
 extern "C" const char *b2_status_string(b2_status s) {
   switch (s) {
@@ -490,8 +449,9 @@ extern "C" const char *b2_status_string(b2_status s) {
     case B2_ERR_CAPACITY: return "token count exceeds capacity";
     case B2_ERR_DEVICE: return "device-side error recorded";
     case B2_ERR_NO_DEVICE: return "no sm_100 device";
+    case B2_ERR_COMM: return "communication error or timeout";
   }
   return "unknown";
 }
 
-extern "C" const char *b2_version(void) { return "b2moe sm_100a tcgen05 v0.1"; }
+extern "C" const char *b2_version(void) { return "b2moe sm_100a tcgen05 v0.2"; }

@@ -1,0 +1,612 @@
+// ep.cu -- expert-parallel MoE layer (include/b2moe_ep.h).
+//
+// Per forward on every rank:
+//   1. route / scan / scatter the local tokens (moe_route_stage): rows in
+//      expert order in sorted_x, per-expert counts on the device;
+//   2. all-gather the [world][E] count matrix; one bounded host wait, then every
+//      rank computes the same exchange plan (b2_ep_plan_compute);
+//   3. dispatch: the copy engine pushes each peer's contiguous chunk of bf16
+//      rows straight into that peer's receive buffer (CUDA IPC mapping over
+//      NVLink), followed by a sequence-number flag -- no SMs are used;
+//   4. the rank's own rows go through the two grouped tcgen05 GEMMs in place
+//      while rows travel; then, per source, a bounded flag wait and the GEMMs
+//      on what arrived;
+//   5. return: each source's results go back the same way into the source's
+//      sout at the rows they came from, so the local k-ordered combine
+//      (moe_combine_stage) reads them unchanged.
+// NCCL (loaded at run time: the process's libnccl.so.2, normally PyTorch's, so
+// the library has no link-time NCCL dependency) carries only the per-forward
+// all-gather of the expert counts and the start-up exchange of IPC handles.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "../../include/b2moe_ep.h"
+#include "moe_internal.h"
+
+using namespace b2;
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char *(*GetErrorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi &nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+#define B2_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+    B2_SYM(GetUniqueId, "ncclGetUniqueId");
+    B2_SYM(CommInitRank, "ncclCommInitRank");
+    B2_SYM(CommDestroy, "ncclCommDestroy");
+    B2_SYM(CommAbort, "ncclCommAbort");
+    B2_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+    B2_SYM(GroupStart, "ncclGroupStart");
+    B2_SYM(GroupEnd, "ncclGroupEnd");
+    B2_SYM(Send, "ncclSend");
+    B2_SYM(Recv, "ncclRecv");
+    B2_SYM(AllGather, "ncclAllGather");
+    B2_SYM(GetErrorString, "ncclGetErrorString");
+#undef B2_SYM
+    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommAbort &&
+             api.CommGetAsyncError && api.GroupStart && api.GroupEnd && api.Send && api.Recv &&
+             api.AllGather && api.GetErrorString;
+  });
+  return api;
+}
+
+#define B2_NCCL(call)                                                                  \
+  do {                                                                                 \
+    ncclResult_t r_ = (call);                                                          \
+    if (r_ != ncclSuccess) {                                                           \
+      fprintf(stderr, "[b2moe] %s failed: %s\n", #call, nccl().GetErrorString(r_));    \
+      return B2_ERR_COMM;                                                              \
+    }                                                                                  \
+  } while (0)
+
+// rows of source s (its expert-sorted order) whose global slot is < g
+int64_t rows_below(const int32_t *cnt_s, const int64_t *gpos_s, int E, int64_t g) {
+  int64_t n = 0;
+  for (int e = 0; e < E; ++e) {
+    const int64_t v = g - gpos_s[e];
+    n += v <= 0 ? 0 : (v < cnt_s[e] ? v : cnt_s[e]);
+  }
+  return n;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- plan
+extern "C" b2_status b2_ep_plan_compute(int G, int r, int E, int mode, const int32_t *cnt,
+                                        b2_ep_plan *p) {
+  if (G < 1 || G > B2_EP_MAX_WORLD || r < 0 || r >= G || E < 1 || !cnt || !p)
+    return B2_ERR_INVALID;
+  if (mode != B2_EP_OWNER && mode != B2_EP_BALANCED) return B2_ERR_INVALID;
+  if (mode == B2_EP_OWNER && E % G != 0) return B2_ERR_INVALID;
+  for (int i = 0; i < G * E; ++i)
+    if (cnt[i] < 0) return B2_ERR_INVALID;
+  memset(p, 0, sizeof(*p));
+  const int32_t *mine = cnt + (size_t)r * E;
+  if (mode == B2_EP_OWNER) {
+    const int EL = E / G;
+    int64_t off = 0;
+    for (int d = 0; d < G; ++d) {  // my rows of rank d's experts are contiguous
+      int64_t c = 0;
+      for (int e = d * EL; e < (d + 1) * EL; ++e) c += mine[e];
+      p->send_off[d] = off;
+      p->send_cnt[d] = c;
+      off += c;
+    }
+    int64_t roff = 0;
+    for (int s = 0; s < G; ++s) {
+      int64_t c = 0;
+      for (int e = r * EL; e < (r + 1) * EL; ++e) c += cnt[(size_t)s * E + e];
+      p->recv_off[s] = roff;
+      p->recv_cnt[s] = c;
+      roff += c;
+    }
+    p->recv_rows = roff;
+    int n = 0;
+    for (int el = 0; el < EL; ++el)  // expert-major, then source
+      for (int s = 0; s < G; ++s) {
+        const int e = r * EL + el;
+        const int32_t c = cnt[(size_t)s * E + e];
+        if (c == 0) continue;
+        int64_t within = 0;
+        for (int e2 = r * EL; e2 < e; ++e2) within += cnt[(size_t)s * E + e2];
+        if (n >= B2_EP_MAX_SEGMENTS) return B2_ERR_INVALID;
+        p->seg_off[n] = (int32_t)(p->recv_off[s] + within);
+        p->seg_cnt[n] = c;
+        p->seg_expert[n] = el;
+        p->seg_source[n] = s;
+        ++n;
+      }
+    p->num_segments = n;
+    return B2_OK;
+  }
+  // ---- balanced: global order is expert-major, then source rank, then the
+  // source's own order; rank d computes global rows [bound[d], bound[d+1]).
+  std::vector<int64_t> tot(E, 0), gpos((size_t)G * E);
+  int64_t R = 0;
+  for (int e = 0; e < E; ++e) {
+    for (int s = 0; s < G; ++s) tot[e] += cnt[(size_t)s * E + e];
+  }
+  int64_t gstart = 0;
+  for (int e = 0; e < E; ++e) {
+    int64_t run = gstart;
+    for (int s = 0; s < G; ++s) {
+      gpos[(size_t)s * E + e] = run;
+      run += cnt[(size_t)s * E + e];
+    }
+    gstart += tot[e];
+  }
+  R = gstart;
+  std::vector<int64_t> bound(G + 1);
+  for (int d = 0; d <= G; ++d) bound[d] = R * d / G;
+  const int64_t *gpos_r = &gpos[(size_t)r * E];
+  for (int d = 0; d < G; ++d) {
+    const int64_t lo = rows_below(mine, gpos_r, E, bound[d]);
+    const int64_t hi = rows_below(mine, gpos_r, E, bound[d + 1]);
+    p->send_off[d] = lo;
+    p->send_cnt[d] = hi - lo;
+  }
+  int64_t roff = 0;
+  std::vector<int64_t> first(G);
+  for (int s = 0; s < G; ++s) {
+    const int32_t *cs = cnt + (size_t)s * E;
+    const int64_t *gs = &gpos[(size_t)s * E];
+    first[s] = rows_below(cs, gs, E, bound[r]);
+    const int64_t c = rows_below(cs, gs, E, bound[r + 1]) - first[s];
+    p->recv_off[s] = roff;
+    p->recv_cnt[s] = c;
+    roff += c;
+  }
+  p->recv_rows = roff;
+  int n = 0;
+  for (int e = 0; e < E; ++e)
+    for (int s = 0; s < G; ++s) {
+      const int32_t *cs = cnt + (size_t)s * E;
+      const int64_t *gs = &gpos[(size_t)s * E];
+      const int64_t a = std::max(gs[e], bound[r]);
+      const int64_t b = std::min(gs[e] + cs[e], bound[r + 1]);
+      if (a >= b) continue;
+      if (n >= B2_EP_MAX_SEGMENTS) return B2_ERR_INVALID;
+      p->seg_off[n] = (int32_t)(p->recv_off[s] + rows_below(cs, gs, E, a) - first[s]);
+      p->seg_cnt[n] = (int32_t)(b - a);
+      p->seg_expert[n] = e;
+      p->seg_source[n] = s;
+      ++n;
+    }
+  p->num_segments = n;
+  return B2_OK;
+}
+
+// ---------------------------------------------------------------- object
+// Flags each rank receives: slot [kFlagDispatch*G + s] is written by rank s's
+// copy engine after its rows landed in our receive buffer; slot
+// [kFlagReturn*G + d] after rank d returned our rows into our sout.  Values are
+// the forward's sequence number, so they never need resetting.
+static constexpr int kFlagDispatch = 0, kFlagReturn = 1;
+
+struct b2_ep {
+  b2_moe *moe = nullptr;
+  int world = 1, rank = 0, mode = 0, E = 0, n_wexp = 0;
+  ncclComm_t comm = nullptr;  // count all-gather (the per-forward barrier) and set-up
+  bool comm_ok = false;
+  cudaStream_t st_d = nullptr, st_r = nullptr;  // copy-engine streams: dispatch / return
+  std::vector<cudaEvent_t> ev_out;               // per exchange step
+  cudaEvent_t ev_ready = nullptr, ev_ret = nullptr;
+  int64_t cap_rows = 0;
+  void *recv_x = nullptr, *inter = nullptr, *out_recv = nullptr;
+  uint64_t *flags = nullptr;                     // [2][world]
+  uint64_t *d_seq = nullptr, *h_seq = nullptr;   // value the copy engines write into flags
+  uint64_t seq = 0;
+  std::vector<char *> peer_recv, peer_sout;      // IPC mappings of the peers' buffers
+  std::vector<uint64_t *> peer_flags;
+  int *d_wait_idx = nullptr, *h_wait_idx = nullptr;
+  CUtensorMap tm_recv, tm_inter;
+  int32_t *d_cnt_all = nullptr, *h_cnt_all = nullptr;
+  int32_t *d_sched = nullptr, *h_sched = nullptr;  // per source: counts|offsets|mtile|group_b
+  std::vector<b2_ep_plan> plans;                   // every rank's plan of the last forward
+  double timeout_s = 60.0;
+};
+
+static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
+
+// Bounded wait, on this GPU, for flags[idx[i]] >= target (one lane per flag).
+// Gives up after timeout_ns, recording kDevTimeoutPeer in *status.
+static __global__ void wait_flags_kernel(const volatile uint64_t *flags, const int *idx, int n,
+                                         uint64_t target, uint64_t timeout_ns, int *status) {
+  const int i = threadIdx.x;
+  if (i < n) {
+    const uint64_t t0 = globaltimer();
+    while (flags[idx[i]] < target) {
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicCAS(status, 0, (int)kDevTimeoutPeer);
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+  __threadfence_system();
+}
+
+extern "C" b2_status b2_ep_unique_id(void *id_out) {
+  if (!id_out) return B2_ERR_INVALID;
+  if (!nccl().ok) return B2_ERR_COMM;
+  ncclUniqueId id;
+  B2_NCCL(nccl().GetUniqueId(&id));
+  memcpy(id_out, &id, sizeof(id));
+  return B2_OK;
+}
+
+static void ep_abort(b2_ep *ep) {
+  if (ep->comm) nccl().CommAbort(ep->comm);
+  ep->comm = nullptr;
+  ep->comm_ok = false;
+}
+
+// Wait for `s` with a bound; abort the communicator if a peer is lost.
+static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return B2_OK;
+    if (q != cudaErrorNotReady) {
+      fprintf(stderr, "[b2moe] stream error: %s\n", cudaGetErrorString(q));
+      return B2_ERR_CUDA;
+    }
+    ncclResult_t ae = ncclSuccess;
+    if (nccl().CommGetAsyncError(ep->comm, &ae) != ncclSuccess || ae != ncclSuccess) {
+      ep_abort(ep);
+      return B2_ERR_COMM;
+    }
+    const double el =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > ep->timeout_s) {
+      fprintf(stderr, "[b2moe] rank %d: peers did not answer within %.1f s; aborting\n",
+              ep->rank, ep->timeout_s);
+      ep_abort(ep);
+      return B2_ERR_COMM;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
+  if (!ep) return B2_OK;
+  if (ep->comm_ok && ep->world > 1 && ep->moe) {
+    // every rank stops using the others' memory before anyone unmaps it
+    cudaStream_t s = ep->st_d;
+    if (nccl().AllGather(ep->moe->counts, ep->d_cnt_all, ep->E, ncclInt32, ep->comm, s) ==
+        ncclSuccess)
+      bounded_sync(ep, s);
+  }
+  if (ep->st_d) cudaStreamSynchronize(ep->st_d);
+  if (ep->st_r) cudaStreamSynchronize(ep->st_r);
+  for (char *p : ep->peer_recv)
+    if (p) cudaIpcCloseMemHandle(p);
+  for (char *p : ep->peer_sout)
+    if (p) cudaIpcCloseMemHandle(p);
+  for (uint64_t *p : ep->peer_flags)
+    if (p) cudaIpcCloseMemHandle(p);
+  if (ep->comm) {
+    if (ep->comm_ok)
+      nccl().CommDestroy(ep->comm);
+    else
+      nccl().CommAbort(ep->comm);
+  }
+  for (cudaEvent_t e : ep->ev_out) cudaEventDestroy(e);
+  if (ep->ev_ready) cudaEventDestroy(ep->ev_ready);
+  if (ep->ev_ret) cudaEventDestroy(ep->ev_ret);
+  if (ep->st_d) cudaStreamDestroy(ep->st_d);
+  if (ep->st_r) cudaStreamDestroy(ep->st_r);
+  if (ep->h_cnt_all) cudaFreeHost(ep->h_cnt_all);
+  if (ep->h_sched) cudaFreeHost(ep->h_sched);
+  if (ep->h_seq) cudaFreeHost(ep->h_seq);
+  if (ep->h_wait_idx) cudaFreeHost(ep->h_wait_idx);
+  b2_moe_destroy(ep->moe);  // also frees the buffers registered with it
+  delete ep;
+  return B2_OK;
+}
+
+extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
+                                  const void *unique_id, int mode, const float *const *w1,
+                                  const float *const *w2, const float *const *w3,
+                                  const float *gate, const float *bias, int weights_on_host,
+                                  b2_stream stream_, b2_ep **out) {
+  if (!desc || !unique_id || !out || world < 1 || world > B2_EP_MAX_WORLD || rank < 0 ||
+      rank >= world)
+    return B2_ERR_INVALID;
+  if (mode != B2_EP_OWNER && mode != B2_EP_BALANCED) return B2_ERR_INVALID;
+  const int E = desc->num_experts;
+  if (mode == B2_EP_OWNER && E % world != 0) return B2_ERR_INVALID;
+  if (!nccl().ok) return B2_ERR_COMM;
+  *out = nullptr;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  b2_ep *ep = new b2_ep();
+  ep->world = world;
+  ep->rank = rank;
+  ep->mode = mode;
+  ep->E = E;
+  ep->n_wexp = mode == B2_EP_OWNER ? E / world : E;
+  b2_status st = moe_create_impl(desc, ep->n_wexp, w1, w2, w3, gate, bias, weights_on_host,
+                                 stream, false, &ep->moe);
+  if (st != B2_OK) {
+    delete ep;
+    return st;
+  }
+  b2_moe *m = ep->moe;
+  const int H = desc->hidden, Ip = m->Ip;
+  const size_t es = m->tf32 ? 4 : 2;
+  const int64_t local_rows = (int64_t)desc->max_tokens * desc->top_k;
+  // receive-side rows; the inter buffer also holds the rank's own rows, which
+  // are computed in place at their expert-sorted positions
+  ep->cap_rows = mode == B2_EP_OWNER ? local_rows * world : local_rows + world;
+  const int64_t inter_rows = std::max<int64_t>(ep->cap_rows, local_rows);
+  auto fail = [&](b2_status s) {
+    b2_ep_destroy(ep);
+    return s;
+  };
+  if ((st = moe_alloc(m, &ep->recv_x, es * ep->cap_rows * H)) != B2_OK) return fail(st);
+  if ((st = moe_alloc(m, &ep->inter, es * inter_rows * Ip)) != B2_OK) return fail(st);
+  if ((st = moe_alloc(m, &ep->out_recv, es * ep->cap_rows * H)) != B2_OK) return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->flags, sizeof(uint64_t) * 2 * world)) != B2_OK)
+    return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_seq, sizeof(uint64_t))) != B2_OK) return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_wait_idx, sizeof(int) * 2 * world)) != B2_OK)
+    return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_cnt_all, sizeof(int32_t) * world * kMaxExperts)) != B2_OK)
+    return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_sched, sizeof(int32_t) * kSchedInts * world)) != B2_OK)
+    return fail(st);
+  if (cudaMallocHost(&ep->h_cnt_all, sizeof(int32_t) * world * kMaxExperts) != cudaSuccess ||
+      cudaMallocHost(&ep->h_sched, sizeof(int32_t) * kSchedInts * world) != cudaSuccess ||
+      cudaMallocHost(&ep->h_seq, sizeof(uint64_t)) != cudaSuccess ||
+      cudaMallocHost(&ep->h_wait_idx, sizeof(int) * 2 * world) != cudaSuccess)
+    return fail(B2_ERR_CUDA);
+  if (cudaMemsetAsync(ep->inter, 0, es * inter_rows * Ip, stream) != cudaSuccess ||
+      cudaMemsetAsync(ep->flags, 0, sizeof(uint64_t) * 2 * world, stream) != cudaSuccess)
+    return fail(B2_ERR_CUDA);
+  const bool f = m->tf32;
+  if (!make_tmap(&ep->tm_recv, ep->recv_x, f, H, ep->cap_rows, (uint64_t)H * es, kBM) ||
+      !make_tmap(&ep->tm_inter, ep->inter, f, Ip, inter_rows, (uint64_t)Ip * es, kBM))
+    return fail(B2_ERR_CUDA);
+  if (cudaStreamCreateWithFlags(&ep->st_d, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ep->st_r, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_ready, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_ret, cudaEventDisableTiming) != cudaSuccess)
+    return fail(B2_ERR_CUDA);
+  ep->ev_out.resize(world, nullptr);
+  for (int k = 0; k < world; ++k)
+    if (cudaEventCreateWithFlags(&ep->ev_out[k], cudaEventDisableTiming) != cudaSuccess)
+      return fail(B2_ERR_CUDA);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return fail(B2_ERR_CUDA);
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  if (nccl().CommInitRank(&ep->comm, world, id, rank) != ncclSuccess) {
+    ep->comm = nullptr;
+    return fail(B2_ERR_COMM);
+  }
+  ep->comm_ok = true;
+  ep->plans.resize(world);
+  // share IPC handles of the receive buffer, sout and the flag words
+  ep->peer_recv.assign(world, nullptr);
+  ep->peer_sout.assign(world, nullptr);
+  ep->peer_flags.assign(world, nullptr);
+  if (world > 1) {
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    std::vector<char> mine(3 * kH), all(3 * kH * world);
+    if (cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(&mine[0]), ep->recv_x) !=
+            cudaSuccess ||
+        cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(&mine[kH]), m->sout) !=
+            cudaSuccess ||
+        cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(&mine[2 * kH]), ep->flags) !=
+            cudaSuccess)
+      return fail(B2_ERR_CUDA);
+    void *d_h = nullptr;
+    if ((st = moe_alloc(m, &d_h, 3 * kH * world)) != B2_OK) return fail(st);
+    if (cudaMemcpyAsync(static_cast<char *>(d_h) + 3 * kH * rank, mine.data(), 3 * kH,
+                        cudaMemcpyHostToDevice, stream) != cudaSuccess)
+      return fail(B2_ERR_CUDA);
+    if (nccl().AllGather(static_cast<char *>(d_h) + 3 * kH * rank, d_h, 3 * kH, ncclUint8,
+                         ep->comm, stream) != ncclSuccess)
+      return fail(B2_ERR_COMM);
+    if (cudaMemcpyAsync(all.data(), d_h, 3 * kH * world, cudaMemcpyDeviceToHost, stream) !=
+        cudaSuccess)
+      return fail(B2_ERR_CUDA);
+    if ((st = bounded_sync(ep, stream)) != B2_OK) return fail(st);
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      cudaIpcMemHandle_t h;
+      void *ptr = nullptr;
+      memcpy(&h, &all[3 * kH * p], kH);
+      if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return fail(B2_ERR_CUDA);
+      ep->peer_recv[p] = static_cast<char *>(ptr);
+      memcpy(&h, &all[3 * kH * p + kH], kH);
+      if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return fail(B2_ERR_CUDA);
+      ep->peer_sout[p] = static_cast<char *>(ptr);
+      memcpy(&h, &all[3 * kH * p + 2 * kH], kH);
+      if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return fail(B2_ERR_CUDA);
+      ep->peer_flags[p] = static_cast<uint64_t *>(ptr);
+    }
+  }
+  *out = ep;
+  return B2_OK;
+}
+
+// GEMM schedule of the segments that came from `src` (rows of the receive
+// buffer), or of the rank's own rows at their expert-sorted positions when
+// `self_rows` is set.  Returns the number of segments.
+static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self_base,
+                      int32_t *h, int *mtiles) {
+  int32_t *hc = h, *ho = h + (kMaxGroups + 1), *hm = ho + (kMaxGroups + 1),
+          *hg = hm + (kMaxGroups + 1);
+  int n = 0, mt = 0;
+  for (int g = 0; g < p.num_segments; ++g) {
+    if (p.seg_source[g] != src) continue;
+    hc[n] = p.seg_cnt[g];
+    ho[n] = self_rows ? (int32_t)(self_base + p.seg_off[g] - p.recv_off[src]) : p.seg_off[g];
+    hg[n] = p.seg_expert[g];
+    hm[n] = mt;
+    mt += (p.seg_cnt[g] + kBM - 1) / kBM;
+    ++n;
+  }
+  hm[n] = mt;
+  *mtiles = mt;
+  return n;
+}
+
+extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
+                                   b2_stream stream_) {
+  if (!ep || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (!ep->comm_ok) return B2_ERR_COMM;
+  b2_moe *m = ep->moe;
+  if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  const int E = ep->E, G = ep->world, r = ep->rank, H = m->d.hidden;
+  const size_t rb = (m->tf32 ? 4 : 2) * (size_t)H;  // bytes per row
+  const uint64_t timeout_ns = (uint64_t)(ep->timeout_s * 1e9);
+
+  // 1. local routing (also for T == 0: the rank still takes part in the exchange)
+  if (T > 0) {
+    B2_RETURN_IF(moe_route_stage(m, x, T, nullptr, s));
+  } else {
+    for (int i = 0; i < 3; ++i) prof_mark(m, s);  // keep the stage-event layout
+    B2_CUDA(cudaMemsetAsync(m->counts, 0, sizeof(int) * E, s));
+  }
+  prof_mark(m, s);  // exchange + expert GEMMs start
+  // 2. count matrix -> host.  The all-gather completes only after every rank's
+  // previous forward finished on its stream, so after this point every peer
+  // buffer written below is free for this forward.
+  B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->comm, s));
+  B2_CUDA(cudaMemcpyAsync(ep->h_cnt_all, ep->d_cnt_all, sizeof(int32_t) * G * E,
+                          cudaMemcpyDeviceToHost, s));
+  B2_RETURN_IF(bounded_sync(ep, s));
+  for (int q = 0; q < G; ++q)
+    B2_RETURN_IF(b2_ep_plan_compute(G, q, E, ep->mode, ep->h_cnt_all, &ep->plans[q]));
+  const b2_ep_plan &p = ep->plans[r];
+  if (p.recv_rows > ep->cap_rows) return B2_ERR_CAPACITY;
+  std::vector<int> nseg(G), mtiles(G);
+  for (int src = 0; src < G; ++src)
+    nseg[src] = fill_sched(p, src, src == r, p.send_off[r], ep->h_sched + (size_t)src * kSchedInts,
+                           &mtiles[src]);
+  int nwait_ret = 0;
+  for (int d = 0; d < G; ++d)
+    if (d != r && p.send_cnt[d] > 0) ep->h_wait_idx[G + nwait_ret++] = kFlagReturn * G + d;
+  ep->seq += 1;
+  *ep->h_seq = ep->seq;
+  B2_CUDA(cudaMemcpyAsync(ep->d_sched, ep->h_sched, sizeof(int32_t) * kSchedInts * G,
+                          cudaMemcpyHostToDevice, s));
+  B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+  for (int src = 0; src < G; ++src) ep->h_wait_idx[src] = kFlagDispatch * G + src;
+  B2_CUDA(cudaMemcpyAsync(ep->d_wait_idx, ep->h_wait_idx, sizeof(int) * 2 * G,
+                          cudaMemcpyHostToDevice, s));
+  B2_CUDA(cudaEventRecord(ep->ev_ready, s));
+
+  auto sched_of = [&](int src) {
+    GemmSched sc;
+    int32_t *d = ep->d_sched + (size_t)src * kSchedInts;
+    sc.counts = d;
+    sc.offsets = d + (kMaxGroups + 1);
+    sc.mtile_offsets = d + 2 * (kMaxGroups + 1);
+    sc.group_b = d + 3 * (kMaxGroups + 1);
+    sc.num_groups = nseg[src];
+    sc.mtiles_upper_bound = mtiles[src];
+    return sc;
+  };
+
+  // 3. dispatch on the copy engine: step k pushes the rows for rank r+k into
+  // its receive buffer, then our sequence number into its flag slot
+  const char *sx = reinterpret_cast<const char *>(m->sorted_x);
+  B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_ready, 0));
+  for (int k = 1; k < G; ++k) {
+    const int to = (r + k) % G;
+    if (p.send_cnt[to])
+      B2_CUDA(cudaMemcpyAsync(ep->peer_recv[to] + ep->plans[to].recv_off[r] * rb,
+                              sx + p.send_off[to] * rb, p.send_cnt[to] * rb,
+                              cudaMemcpyDeviceToDevice, ep->st_d));
+    B2_CUDA(cudaMemcpyAsync(ep->peer_flags[to] + kFlagDispatch * G + r, ep->d_seq,
+                            sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_d));
+  }
+  // 4. own rows first, in place (sorted_x -> inter -> sout), while rows travel
+  if (nseg[r] > 0)
+    B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(r), s,
+                                false));
+  // 5. per step: wait for the rows of rank r-k, expert GEMMs, return them
+  const char *ro = reinterpret_cast<const char *>(ep->out_recv);
+  for (int k = 1; k < G; ++k) {
+    const int from = (r - k + G) % G;
+    if (p.recv_cnt[from] > 0) {
+      wait_flags_kernel<<<1, 32, 0, s>>>(ep->flags, ep->d_wait_idx + from, 1, ep->seq, timeout_ns,
+                                         m->status);
+      B2_LAUNCHED();
+      B2_RETURN_IF(moe_gemm_stage(m, ep->tm_recv, ep->tm_inter, ep->inter, ep->out_recv,
+                                  sched_of(from), s, false));
+    }
+    B2_CUDA(cudaEventRecord(ep->ev_out[k], s));
+    B2_CUDA(cudaStreamWaitEvent(ep->st_r, ep->ev_out[k], 0));
+    if (p.recv_cnt[from])
+      B2_CUDA(cudaMemcpyAsync(ep->peer_sout[from] + ep->plans[from].send_off[r] * rb,
+                              ro + p.recv_off[from] * rb, p.recv_cnt[from] * rb,
+                              cudaMemcpyDeviceToDevice, ep->st_r));
+    B2_CUDA(cudaMemcpyAsync(ep->peer_flags[from] + kFlagReturn * G + r, ep->d_seq,
+                            sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_r));
+  }
+  prof_mark(m, s);  // expert GEMMs done; waiting for returns
+  if (nwait_ret > 0) {
+    wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(
+        ep->flags, ep->d_wait_idx + G, nwait_ret, ep->seq, timeout_ns, m->status);
+    B2_LAUNCHED();
+  }
+  if (G > 1) {
+    // our own copy streams are done before the next forward reuses the sources
+    B2_CUDA(cudaEventRecord(ep->ev_ret, ep->st_r));
+    B2_CUDA(cudaStreamWaitEvent(s, ep->ev_ret, 0));
+  }
+  // 6. local k-ordered combine
+  if (T > 0) {
+    B2_RETURN_IF(moe_combine_stage(m, y, T, s));
+  } else {
+    for (int i = 0; i < 2; ++i) prof_mark(m, s);
+  }
+  return B2_OK;
+}
+
+extern "C" b2_status b2_ep_set_timeout(b2_ep *ep, double seconds) {
+  if (!ep || !(seconds > 0)) return B2_ERR_INVALID;
+  ep->timeout_s = seconds;
+  return B2_OK;
+}
+
+extern "C" b2_status b2_ep_last_plan(const b2_ep *ep, b2_ep_plan *plan) {
+  if (!ep || !plan) return B2_ERR_INVALID;
+  *plan = ep->plans.empty() ? b2_ep_plan{} : ep->plans[ep->rank];
+  return B2_OK;
+}
+
+extern "C" b2_moe *b2_ep_layer(b2_ep *ep) { return ep ? ep->moe : nullptr; }

@@ -44,6 +44,7 @@ struct GemmArgs {
   const int *counts;         // grouped: rows per group
   const int *offsets;        // grouped: first row of each group in A / C
   const int *mtile_offsets;  // grouped: exclusive prefix of ceil(count/128), [G+1]
+  const int *group_b;        // grouped, optional: B block of each group (default: the group index)
   int num_groups;            // grouped: G (<= kMaxGroups); dense: 0
   int b_rows_per_group;      // grouped: rows of B per group
   int M;                     // dense rows
@@ -57,7 +58,7 @@ struct GemmArgs {
 };
 
 constexpr size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kStages * (kABytes + kBBytes) + 256 + 3 * (kMaxGroups + 1) * 4;
+  return 1024 + (size_t)kStages * (kABytes + kBBytes) + 256 + 4 * (kMaxGroups + 1) * 4;
 }
 
 struct TileInfo {
@@ -66,7 +67,8 @@ struct TileInfo {
 
 __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
                                                 const int *s_mt, const int *s_off,
-                                                const int *s_cnt, int out_tile_cols) {
+                                                const int *s_cnt, const int *s_grp,
+                                                int out_tile_cols) {
   TileInfo t;
   const int NT = g.num_n_tiles;
   if (g.num_groups > 0) {
@@ -80,7 +82,7 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
     const int m = gm - s_mt[lo];
     t.a_row = s_off[lo] + m * kBM;
     t.rows_valid = min(kBM, s_cnt[lo] - m * kBM);
-    t.b_row = lo * g.b_rows_per_group + n * kBN;
+    t.b_row = s_grp[lo] * g.b_rows_per_group + n * kBN;
     t.n_tile = n;
   } else {
     const int MT = (g.M + kBM - 1) / kBM;
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int *s_mt = reinterpret_cast<int *>(bars) + 64;  // 256 B past the barrier block
   int *s_off = s_mt + (kMaxGroups + 1);
   int *s_cnt = s_off + (kMaxGroups + 1);
+  int *s_grp = s_cnt + (kMaxGroups + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -189,6 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (i < g.num_groups) {
         s_off[i] = g.offsets[i];
         s_cnt[i] = g.counts[i];
+        s_grp[i] = g.group_b ? g.group_b[i] : i;
       }
     }
   }
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued = 0;
       uint32_t last_par = 0;
       for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-        const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, out_tile_cols);
+        const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols);
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, g.status,
@@ -295,7 +299,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_par = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, out_tile_cols);
+      const TileInfo t = decode_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols);
       if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue))
         break;
       tc_fence_after();

@@ -1,0 +1,142 @@
+// moe_internal.h -- the MoE layer object and its pipeline stages, shared by
+// the single-GPU entry points (b2moe_api.cu) and the expert-parallel ones
+// (ep.cu).  Host code; not part of the public C ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <vector>
+
+#include "../../include/b2moe.h"
+#include "gemm_sm100.cuh"
+#include "host_tmap.h"
+#include "moe_kernels.cuh"
+
+namespace b2 {
+
+// number of this library's kernel launches (all devices, whole process)
+std::atomic<uint64_t> &launch_counter();
+
+#define B2_CUDA(call)                                                                  \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess) {                                                           \
+      fprintf(stderr, "[b2moe] %s failed at %s:%d: %s\n", #call, __FILE__, __LINE__,   \
+              cudaGetErrorString(e_));                                                 \
+      return B2_ERR_CUDA;                                                              \
+    }                                                                                  \
+  } while (0)
+
+#define B2_LAUNCHED()                                                    \
+  do {                                                                   \
+    ::b2::launch_counter().fetch_add(1, std::memory_order_relaxed);      \
+    B2_CUDA(cudaGetLastError());                                         \
+  } while (0)
+
+#define B2_RETURN_IF(x)     \
+  do {                      \
+    b2_status s_ = (x);     \
+    if (s_ != B2_OK) return s_; \
+  } while (0)
+
+struct DevInfo {
+  int sms = 0;
+  int cc_major = 0;
+};
+
+inline bool dev_info(DevInfo *d) {
+  int dev;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return false;
+  if (cudaDeviceGetAttribute(&d->cc_major, cudaDevAttrComputeCapabilityMajor, dev) !=
+      cudaSuccess)
+    return false;
+  return true;
+}
+
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
+                      int grid, cudaStream_t s) {
+  auto kern = gemm_sm100_kernel<EPI, TF32, TOut>;
+  const size_t smem = gemm_smem_bytes();
+  // per-device attribute; cheap enough to set on every launch
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (grid <= 0) return B2_OK;
+  kern<<<grid, kGemmThreads, smem, s>>>(ta, tb, args);
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
+// Row segments the two grouped GEMMs run over: group g covers rows
+// [offsets[g], offsets[g] + counts[g]) of A and C and multiplies them with
+// expert block group_b[g] (or g when group_b is null) of the weights.
+struct GemmSched {
+  const int *counts = nullptr;
+  const int *offsets = nullptr;
+  const int *mtile_offsets = nullptr;  // exclusive prefix of ceil(count/128), [groups+1]
+  const int *group_b = nullptr;
+  int num_groups = 0;
+  long long mtiles_upper_bound = 0;    // sizes the persistent grid
+};
+
+}  // namespace b2
+
+// ---------------------------------------------------------------- the layer
+struct b2_moe {
+  b2_moe_desc d;          // router / layer shape (num_experts = router experts)
+  int n_wexp = 0;         // experts whose weights this object holds
+  int device = 0;
+  int Ip = 0;             // inter padded to 128
+  int sms = 0;
+  bool tf32 = false;
+  size_t bytes = 0;
+  // weights
+  float *gateT = nullptr;
+  float *bias = nullptr;
+  void *w13 = nullptr;    // [n_wexp][2Ip][H]
+  void *w2 = nullptr;     // [n_wexp][H][Ip]
+  // scratch
+  int *topk_idx = nullptr, *block_counts = nullptr, *block_base = nullptr;
+  int *counts = nullptr, *offsets = nullptr, *mtile = nullptr;
+  int *token_slot = nullptr, *sorted_token = nullptr;
+  float *topk_w = nullptr, *sorted_w = nullptr;
+  void *sorted_x = nullptr, *inter = nullptr, *sout = nullptr;
+  int *status = nullptr;
+  CUtensorMap tm_x, tm_w13, tm_inter, tm_w2;
+  std::vector<void *> allocs;
+  // stage profiling
+  bool profile = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<cudaEvent_t> ev_rec;
+};
+
+namespace b2 {
+
+constexpr int kStageEvents = 7;
+
+// Allocates and packs a layer object.  w1/w2/w3 hold n_wexp expert matrices
+// (those this object computes); desc->num_experts is the router's expert count.
+// local_gemm_buffers = false skips the intermediate buffer sized for the local
+// rows (an expert-parallel owner keeps its intermediates elsewhere).
+b2_status moe_create_impl(const b2_moe_desc *desc, int n_wexp, const float *const *w1,
+                          const float *const *w2, const float *const *w3, const float *gate,
+                          const float *bias, int weights_on_host, cudaStream_t stream,
+                          bool local_gemm_buffers, b2_moe **out);
+b2_status moe_alloc(b2_moe *m, void **p, size_t bytes);
+void prof_mark(b2_moe *m, cudaStream_t s);
+
+// route + scan + scatter of T local tokens into m->sorted_x (expert order)
+b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *tr,
+                          cudaStream_t s);
+// W1||W3 + SwiGLU and W2 over the scheduled row segments of A (rows of tm_a1)
+b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap &tm_a2,
+                         void *inter, void *out, const GemmSched &sched, cudaStream_t s,
+                         bool stage_marks = true);
+// y[t] = sum_k w[t,k] * m->sout[slot(t,k)]
+b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s);
+
+}  // namespace b2

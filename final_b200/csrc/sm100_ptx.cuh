@@ -23,6 +23,7 @@ enum DeviceStatus : int {
   kDevTimeoutMma = 0x102,
   kDevTimeoutEpilogue = 0x103,
   kDevTimeoutDrain = 0x104,
+  kDevTimeoutPeer = 0x105,
   kDevBadExpert = 0x201,
   kDevBadSlot = 0x202,
 };

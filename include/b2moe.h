@@ -30,6 +30,7 @@ typedef enum b2_status {
   B2_ERR_CAPACITY = 3,    /* num_tokens > max_tokens of the object */
   B2_ERR_DEVICE = 4,      /* a kernel recorded a device-side error */
   B2_ERR_NO_DEVICE = 5,   /* no sm_100 device present */
+  B2_ERR_COMM = 6,        /* collective failed or a peer did not answer in time */
 } b2_status;
 
 typedef enum b2_dtype {

@@ -1,0 +1,105 @@
+/*
+ * b2moe_ep.h -- expert-parallel MoE layer over several GPUs of one node
+ * (C ABI).  One process per GPU; token rows travel between GPUs as
+ * copy-engine writes into the peers' buffers (CUDA IPC over NVLink /
+ * NVSwitch), NCCL carries the per-forward count all-gather.
+ *
+ * No counterpart in the reference for the collective path itself: the
+ * reference runs each whole decoder layer on one GPU of a 24-stage pipeline
+ * and moves activations with cudaMemcpyAsync peer copies
+ * (src/model.cu:235-339, 441-468).  b2_ep_forward replaces
+ * SparseMoeBlock::forward_gpu (include/layer.h:80-81) on a rank that holds a
+ * shard of the tokens.
+ *
+ * Placement modes:
+ *   B2_EP_OWNER     rank r holds experts [r*E/G, (r+1)*E/G) (E divisible by G)
+ *                   and computes every row routed to them;
+ *   B2_EP_BALANCED  every rank holds all E experts' weights (705 MB in bf16 for
+ *                   the reference model) and computes an equal contiguous share
+ *                   of the globally expert-sorted rows, which removes the load
+ *                   imbalance of skewed (e.g. Zipf) routing.
+ * Both produce bit-identical y to the single-GPU b2_moe_forward on the same
+ * tokens: every row goes through the same kernels in the same order.
+ */
+#ifndef B2MOE_EP_H
+#define B2MOE_EP_H
+
+#include "b2moe.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2_EP_MAX_WORLD 64
+#define B2_EP_MAX_SEGMENTS 256
+#define B2_EP_UNIQUE_ID_BYTES 128
+
+typedef enum b2_ep_mode { B2_EP_OWNER = 0, B2_EP_BALANCED = 1 } b2_ep_mode;
+
+/* Exchange plan of one rank, computed from the [world][E] matrix of every
+ * rank's per-expert row counts.  Row ranges are in units of rows. */
+typedef struct b2_ep_plan {
+  int64_t send_off[B2_EP_MAX_WORLD]; /* my expert-sorted rows [off, off+cnt) go to rank d */
+  int64_t send_cnt[B2_EP_MAX_WORLD];
+  int64_t recv_off[B2_EP_MAX_WORLD]; /* rows from rank s land at receive row off */
+  int64_t recv_cnt[B2_EP_MAX_WORLD];
+  int64_t recv_rows;                 /* total rows this rank computes */
+  int32_t num_segments;              /* GEMM row segments of the receive buffer */
+  int32_t seg_off[B2_EP_MAX_SEGMENTS];
+  int32_t seg_cnt[B2_EP_MAX_SEGMENTS];
+  int32_t seg_expert[B2_EP_MAX_SEGMENTS]; /* index into this rank's expert weights */
+  int32_t seg_source[B2_EP_MAX_SEGMENTS]; /* rank the segment's rows came from */
+} b2_ep_plan;
+
+typedef struct b2_ep b2_ep;
+
+/* Pure host computation (no GPU): the plan of `rank`.  counts is row-major
+ * [world][num_experts]. */
+b2_status b2_ep_plan_compute(int world, int rank, int num_experts, int mode,
+                             const int32_t *counts, b2_ep_plan *plan);
+
+/* NCCL unique id for the communicator (call on rank 0, share the 128 bytes
+ * with the other ranks, e.g. through torch.distributed). */
+b2_status b2_ep_unique_id(void *id_out);
+
+/* Collective over all ranks.  desc describes the layer as for b2_moe_create
+ * (num_experts = all E experts, max_tokens = this rank's token capacity).
+ * w1/w2/w3 hold the experts this rank computes: E/world pointers for
+ * B2_EP_OWNER (experts rank*E/world ...), all E for B2_EP_BALANCED.  gate and
+ * bias are the full router.  Device or host pointers as in b2_moe_create. */
+b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
+                       const void *unique_id, int mode, const float *const *w1,
+                       const float *const *w2, const float *const *w3,
+                       const float *gate, const float *bias, int weights_on_host,
+                       b2_stream stream, b2_ep **out);
+
+/* Collective.  y[T,H] = MoE(x[T,H]) for this rank's T tokens.  Synchronises
+ * `stream` once to size the exchange (the count all-gather); returns
+ * B2_ERR_COMM if a peer does not answer within the timeout (the communicator
+ * is then aborted).  Rows for rank r+k are pushed by the copy engine into that
+ * rank's receive buffer followed by a sequence-number flag; each rank runs its
+ * own rows through the expert GEMMs in place while rows travel, then each
+ * source's rows after a bounded wait on its flag (a wait that runs out records
+ * a device error readable with b2_moe_get_status on b2_ep_layer), and pushes
+ * the results back the same way. */
+b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int num_tokens,
+                        b2_stream stream);
+
+/* Host-side bound (seconds) on every wait for the peers (default 60). */
+b2_status b2_ep_set_timeout(b2_ep *ep, double seconds);
+
+/* The plan used by the last forward (for tests and load reports). */
+b2_status b2_ep_last_plan(const b2_ep *ep, b2_ep_plan *plan);
+
+/* The single-GPU layer object inside (routing, local scratch, weights);
+ * valid until b2_ep_destroy.  Lets callers use b2_moe_profile_* and
+ * b2_moe_get_status on the expert-parallel layer. */
+b2_moe *b2_ep_layer(b2_ep *ep);
+
+b2_status b2_ep_destroy(b2_ep *ep);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2MOE_EP_H */

@@ -8,8 +8,10 @@ ROOT = Path(__file__).resolve().parent.parent
 
 
 def _declared():
-    text = (ROOT / "include" / "b2moe.h").read_text()
-    return sorted(set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for h in sorted((ROOT / "include").glob("*.h")):
+        names |= set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", h.read_text()))
+    return sorted(names)
 
 
 def test_header_matches_binding_list():

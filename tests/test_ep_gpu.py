@@ -1,0 +1,113 @@
+"""Expert-parallel MoE on GPUs, through the C ABI of include/b2moe_ep.h.
+
+Every rank's output must be bit-identical to the single-GPU layer's output for
+the same tokens: rows meet the same expert in the same kernels, and the
+combine order does not change.  The 2-rank test needs two GPUs and is skipped
+on a one-GPU box (the host-side exchange logic is covered on CPU by
+tests/test_ep_plan.py)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from moe_cases import build_case
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _single_gpu_y(inp, dev):
+    from final_b200 import SparseMoeBlock
+    layer = SparseMoeBlock(_t(inp["gate"], dev), _t(inp["w1"], dev), _t(inp["w2"], dev),
+                           _t(inp["w3"], dev), _t(inp["bias"], dev),
+                           max_tokens=inp["x"].shape[0], top_k=inp["K"])
+    y = layer.forward(_t(inp["x"], dev))
+    torch.cuda.synchronize()
+    layer.close()
+    return y.cpu()
+
+
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+def test_ep_one_rank_matches_single_gpu(cuda_dev, mode):
+    from final_b200.ep import ExpertParallelMoE
+    inp = build_case("zipf")
+    want = _single_gpu_y(inp, cuda_dev)
+    ep = ExpertParallelMoE(_t(inp["gate"], cuda_dev), _t(inp["w1"], cuda_dev),
+                           _t(inp["w2"], cuda_dev), _t(inp["w3"], cuda_dev),
+                           _t(inp["bias"], cuda_dev), max_tokens=inp["x"].shape[0],
+                           top_k=inp["K"], mode=mode, world=1, rank=0)
+    y = ep.forward(_t(inp["x"], cuda_dev))
+    torch.cuda.synchronize()
+    assert ep.device_status() == 0
+    assert torch.equal(y.cpu(), want)
+    plan = ep.last_plan()
+    assert plan["recv_rows"] == inp["x"].shape[0] * inp["K"]
+    # a second forward with fewer tokens reuses the communicator and buffers
+    y2 = ep.forward(_t(inp["x"][:100], cuda_dev))
+    torch.cuda.synchronize()
+    assert torch.equal(y2.cpu(), _single_gpu_y({**inp, "x": inp["x"][:100]}, cuda_dev))
+    ep.close()
+
+
+def _rank_main(rank, world, port, mode, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "oracle"), os.path.join(root, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    from moe_cases import build_case as bc
+    from final_b200.ep import ExpertParallelMoE
+    import datetime
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        inp = bc("zipf")
+        shard = np.array_split(np.arange(inp["x"].shape[0]), world)[rank]
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        ep = ExpertParallelMoE(t(inp["gate"]), t(inp["w1"]), t(inp["w2"]), t(inp["w3"]),
+                               t(inp["bias"]), max_tokens=len(shard), top_k=inp["K"], mode=mode,
+                               timeout_s=60.0)
+        y = ep.forward(t(inp["x"][shard]))
+        torch.cuda.synchronize()
+        status = ep.device_status()
+        plan = ep.last_plan()
+        ep.close()
+        q.put((rank, y.cpu().numpy(), status, plan["recv_rows"]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+def test_ep_two_ranks_match_single_gpu(cuda_dev, mode):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs (host-side exchange logic is tested on CPU)")
+    import torch.multiprocessing as mp
+    inp = build_case("zipf")
+    want = _single_gpu_y(inp, cuda_dev).numpy()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, y, status, rows = q.get(timeout=300)
+        assert status == 0
+        got[r] = y
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    y = np.concatenate([got[0], got[1]])
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))

@@ -1,0 +1,224 @@
+"""Expert-parallel host logic on CPU: the exchange plan (b2_ep_plan_compute,
+the C ABI of include/b2moe_ep.h) and the whole dispatch -> expert FFN ->
+return -> combine dataflow, emulated with the CPU oracle, single-process and
+as two gloo ranks.  The expert-parallel result must equal the single-rank
+result bit for bit: every row meets the same expert and the combine order is
+unchanged."""
+import os
+
+import numpy as np
+import pytest
+
+from final_b200 import ep as epmod
+
+
+def _random_counts(rng, world, E, zipf=False):
+    if zipf:
+        p = np.arange(1, E + 1) ** -1.1
+        p /= p.sum()
+        return np.stack([rng.multinomial(int(rng.integers(0, 400)), p) for _ in range(world)])
+    return rng.integers(0, 60, size=(world, E))
+
+
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("zipf", [False, True])
+def test_plan_invariants(mode, world, zipf):
+    rng = np.random.default_rng(world * 10 + zipf)
+    E = 32
+    for trial in range(5):
+        cnt = _random_counts(rng, world, E, zipf).astype(np.int32)
+        if trial == 0:
+            cnt[:, 3] = 0  # an expert nobody chose
+        plans = [epmod.plan(cnt, r, mode) for r in range(world)]
+        R = int(cnt.sum())
+        assert sum(p["recv_rows"] for p in plans) == R
+        for r, p in enumerate(plans):
+            assert sum(p["send_cnt"]) == int(cnt[r].sum())
+            # sends are contiguous, in rank order, covering my rows
+            assert p["send_off"][0] == 0
+            for d in range(1, world):
+                assert p["send_off"][d] == p["send_off"][d - 1] + p["send_cnt"][d - 1]
+            for s in range(world):
+                assert plans[s]["send_cnt"][r] == p["recv_cnt"][s]
+            # segments tile the receive buffer exactly once
+            cover = np.zeros(p["recv_rows"], dtype=np.int32)
+            for o, c, e in zip(p["seg_off"], p["seg_cnt"], p["seg_expert"]):
+                assert c > 0
+                cover[o:o + c] += 1
+                assert 0 <= e < (E // world if mode == "owner" else E)
+            assert np.all(cover == 1)
+            if mode == "balanced":
+                assert abs(p["recv_rows"] - R / world) <= 1
+
+
+def test_plan_balanced_removes_zipf_skew():
+    rng = np.random.default_rng(0)
+    E, world = 32, 8
+    p = np.arange(1, E + 1) ** -1.1
+    p /= p.sum()
+    cnt = np.stack([rng.multinomial(16384 * 4, p) for _ in range(world)]).astype(np.int32)
+    own = [epmod.plan(cnt, r, "owner")["recv_rows"] for r in range(world)]
+    bal = [epmod.plan(cnt, r, "balanced")["recv_rows"] for r in range(world)]
+    assert max(own) / np.mean(own) > 2.5          # hot experts pile onto rank 0
+    assert max(bal) / np.mean(bal) < 1.0001
+
+
+def test_plan_rejects_bad_input():
+    from final_b200 import B2Error
+    with pytest.raises(B2Error):
+        epmod.plan(np.ones((3, 32), dtype=np.int32), 0, "owner")  # 32 experts on 3 owners
+    with pytest.raises(B2Error):
+        epmod.plan(-np.ones((2, 32), dtype=np.int32), 0, "balanced")
+
+
+# ------------------------------------------------------------------ emulation
+def _rank_route(oracle, x, gate, bias, K):
+    """Local routing + canonical expert-sorted rows, as the GPU route stage."""
+    E = gate.shape[0]
+    logits = oracle.gemm_nt(x, gate)
+    idx, w, counts = oracle.route(logits, bias, K)
+    off, _ = oracle.scan(counts, 128)
+    st, _, slot = oracle.scatter(idx, w, E, off)
+    return dict(idx=idx, w=w, counts=counts, off=off, rows=x[st[:int(counts.sum())]], slot=slot)
+
+
+def _ffn_segments(oracle, recv, segs, w1, w3, w2, mode, rank, world):
+    out = np.zeros((recv.shape[0], w2.shape[1]), dtype=np.float32)
+    el = w1.shape[0] // world
+    for o, c, e in zip(segs["seg_off"], segs["seg_cnt"], segs["seg_expert"]):
+        ge = rank * el + e if mode == "owner" else e
+        sl = recv[o:o + c]
+        res = oracle.expert_ffn(sl, np.arange(c, dtype=np.int32), np.zeros(1, np.int32),
+                                np.array([c], np.int32), w1[ge:ge + 1], w3[ge:ge + 1], w2[ge:ge + 1])
+        out[o:o + c] = res[:c]
+    return out
+
+
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+def test_ep_dataflow_emulated_matches_single_rank(oracle, mode):
+    from moe_cases import build_case
+    inp = build_case("zipf")  # skewed routing, 512 tokens, H=256
+    world, K = 4, inp["K"]
+    T = inp["x"].shape[0]
+    ref = oracle.moe_forward(inp["x"], inp["gate"], inp["bias"], inp["w1"], inp["w2"], inp["w3"], K=K)
+    shards = np.array_split(np.arange(T), world)
+    ranks = [_rank_route(oracle, inp["x"][sh], inp["gate"], inp["bias"], K) for sh in shards]
+    cnt = np.stack([r["counts"] for r in ranks]).astype(np.int32)
+    plans = [epmod.plan(cnt, r, mode) for r in range(world)]
+    # dispatch
+    recv = []
+    for d in range(world):
+        buf = np.zeros((plans[d]["recv_rows"], inp["x"].shape[1]), dtype=np.float32)
+        for s in range(world):
+            o, c = plans[s]["send_off"][d], plans[s]["send_cnt"][d]
+            ro = plans[d]["recv_off"][s]
+            buf[ro:ro + c] = ranks[s]["rows"][o:o + c]
+        recv.append(buf)
+    outs = [_ffn_segments(oracle, recv[d], plans[d], inp["w1"], inp["w3"], inp["w2"], mode, d, world)
+            for d in range(world)]
+    # return + combine
+    ys = []
+    for s in range(world):
+        sout = np.zeros((int(cnt[s].sum()), inp["x"].shape[1]), dtype=np.float32)
+        for d in range(world):
+            o, c = plans[s]["send_off"][d], plans[s]["send_cnt"][d]
+            ro = plans[d]["recv_off"][s]
+            sout[o:o + c] = outs[d][ro:ro + c]
+        ys.append(oracle.combine(sout, ranks[s]["slot"], ranks[s]["w"], inp["x"].shape[1]))
+    y = np.concatenate(ys)
+    assert np.array_equal(y.view(np.uint32), ref["y"].view(np.uint32))
+
+
+# ------------------------------------------------------------------ gloo ranks
+def _gloo_rank(rank, world, port, mode, result_q):
+    import torch
+    import torch.distributed as dist
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "oracle"), os.path.join(root, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import oracle
+    from moe_cases import build_case
+    from final_b200 import ep as epm
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        inp = build_case("ragged")
+        K, H = inp["K"], inp["x"].shape[1]
+        shard = np.array_split(np.arange(inp["x"].shape[0]), world)[rank]
+        loc = _rank_route(oracle, inp["x"][shard], inp["gate"], inp["bias"], K)
+        mine = torch.from_numpy(loc["counts"].astype(np.int32))
+        allc = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allc, mine)
+        cnt = torch.stack(allc).numpy()
+        p = epm.plan(cnt, rank, mode)
+        plans = [epm.plan(cnt, r, mode) for r in range(world)]
+        rows = torch.from_numpy(np.ascontiguousarray(loc["rows"]))
+        recv = torch.zeros(p["recv_rows"], H)
+        reqs = []
+        for d in range(world):
+            o, c = p["send_off"][d], p["send_cnt"][d]
+            if d == rank:
+                recv[p["recv_off"][rank]:p["recv_off"][rank] + c] = rows[o:o + c]
+            elif c:
+                reqs.append(dist.isend(rows[o:o + c].contiguous(), d))
+        for s in range(world):
+            c = p["recv_cnt"][s]
+            if s != rank and c:
+                tmp = torch.zeros(c, H)
+                dist.recv(tmp, s)
+                recv[p["recv_off"][s]:p["recv_off"][s] + c] = tmp
+        for r_ in reqs:
+            r_.wait()
+        out = torch.from_numpy(_ffn_segments(oracle, recv.numpy(), p, inp["w1"], inp["w3"],
+                                             inp["w2"], mode, rank, world))
+        sout = torch.zeros(int(cnt[rank].sum()), H)
+        reqs = []
+        for s in range(world):
+            o, c = p["recv_off"][s], p["recv_cnt"][s]
+            if s == rank:
+                so = p["send_off"][rank]
+                sout[so:so + c] = out[o:o + c]
+            elif c:
+                reqs.append(dist.isend(out[o:o + c].contiguous(), s))
+        for d in range(world):
+            c = p["send_cnt"][d]
+            if d != rank and c:
+                tmp = torch.zeros(c, H)
+                dist.recv(tmp, d)
+                sout[p["send_off"][d]:p["send_off"][d] + c] = tmp
+        for r_ in reqs:
+            r_.wait()
+        y = oracle.combine(sout.numpy(), loc["slot"], loc["w"], H)
+        result_q.put((rank, y, plans[rank]["recv_rows"]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+def test_ep_two_gloo_ranks_match_single_rank(oracle, mode):
+    import socket
+    import torch.multiprocessing as mp
+    from moe_cases import build_case
+    inp = build_case("ragged")
+    ref = oracle.moe_forward(inp["x"], inp["gate"], inp["bias"], inp["w1"], inp["w2"], inp["w3"],
+                             K=inp["K"])
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, y, _rows = q.get(timeout=120)
+        got[r] = y
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    y = np.concatenate([got[0], got[1]])
+    assert np.array_equal(y.view(np.uint32), ref["y"].view(np.uint32))
