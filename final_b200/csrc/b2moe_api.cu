@@ -220,26 +220,26 @@ b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *
   const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden;
   const int nb = (T + kRouteTB - 1) / kRouteTB;
   prof_mark(m, s);
-  route_kernel<<<nb, kRouteThreads, 0, s>>>(x, m->gateT, m->d.use_bias ? m->bias : nullptr, T, H, E,
-                                            K, m->d.routed_scale, m->topk_idx, m->topk_w,
-                                            m->block_counts, tr ? tr->logits : nullptr);
-  B2_LAUNCHED();
+  B2_RETURN_IF(launch_pdl(route_kernel, dim3(nb), dim3(kRouteThreads), 0, s, x,
+                          (const float *)m->gateT, (const float *)(m->d.use_bias ? m->bias : nullptr),
+                          T, H, E, K, m->d.routed_scale, m->topk_idx, m->topk_w, m->block_counts,
+                          tr ? tr->logits : (float *)nullptr));
   prof_mark(m, s);
-  scan_kernel<<<1, 1024, 0, s>>>(m->block_counts, nb, E, kBM, m->counts, m->offsets, m->mtile,
-                                 m->block_base);
-  B2_LAUNCHED();
+  B2_RETURN_IF(launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, s, (const int *)m->block_counts, nb,
+                          E, (int)kBM, m->counts, m->offsets, m->mtile, m->block_base));
   prof_mark(m, s);
   if (m->tf32)
-    scatter_kernel<float><<<nb, scatter_threads(K), 0, s>>>(
-        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
-        reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token, m->sorted_w,
-        m->status);
+    B2_RETURN_IF(launch_pdl(scatter_kernel<float>, dim3(nb), dim3(scatter_threads(K)), 0, s, x,
+                            (const int *)m->topk_idx, (const float *)m->topk_w,
+                            (const int *)m->block_base, T, H, E, K,
+                            reinterpret_cast<float *>(m->sorted_x), m->token_slot, m->sorted_token,
+                            m->sorted_w, m->status));
   else
-    scatter_kernel<__nv_bfloat16><<<nb, scatter_threads(K), 0, s>>>(
-        x, m->topk_idx, m->topk_w, m->block_base, T, H, E, K,
-        reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot, m->sorted_token,
-        m->sorted_w, m->status);
-  B2_LAUNCHED();
+    B2_RETURN_IF(launch_pdl(scatter_kernel<__nv_bfloat16>, dim3(nb), dim3(scatter_threads(K)), 0,
+                            s, x, (const int *)m->topk_idx, (const float *)m->topk_w,
+                            (const int *)m->block_base, T, H, E, K,
+                            reinterpret_cast<__nv_bfloat16 *>(m->sorted_x), m->token_slot,
+                            m->sorted_token, m->sorted_w, m->status));
   return B2_OK;
 }
 
@@ -288,12 +288,13 @@ b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s) {
   const int K = m->d.top_k, H = m->d.hidden;
   prof_mark(m, s);
   if (m->tf32)
-    combine_kernel<float><<<T, 256, 0, s>>>(reinterpret_cast<const float *>(m->sout),
-                                            m->token_slot, m->topk_w, T, H, K, y);
+    B2_RETURN_IF(launch_pdl(combine_kernel<float>, dim3(T), dim3(256), 0, s,
+                            reinterpret_cast<const float *>(m->sout), (const int *)m->token_slot,
+                            (const float *)m->topk_w, T, H, K, y));
   else
-    combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(m->sout), m->token_slot, m->topk_w, T, H, K, y);
-  B2_LAUNCHED();
+    B2_RETURN_IF(launch_pdl(combine_kernel<__nv_bfloat16>, dim3(T), dim3(256), 0, s,
+                            reinterpret_cast<const __nv_bfloat16 *>(m->sout),
+                            (const int *)m->token_slot, (const float *)m->topk_w, T, H, K, y));
   prof_mark(m, s);
   return B2_OK;
 }

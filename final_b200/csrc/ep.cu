@@ -379,10 +379,11 @@ extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
     return fail(st);
   if ((st = moe_alloc(m, (void **)&ep->d_cnt_all, sizeof(int32_t) * world * kMaxExperts)) != B2_OK)
     return fail(st);
-  if ((st = moe_alloc(m, (void **)&ep->d_sched, sizeof(int32_t) * kSchedInts * world)) != B2_OK)
+  if ((st = moe_alloc(m, (void **)&ep->d_sched, sizeof(int32_t) * kSchedInts * (world + 1))) !=
+      B2_OK)
     return fail(st);
   if (cudaMallocHost(&ep->h_cnt_all, sizeof(int32_t) * world * kMaxExperts) != cudaSuccess ||
-      cudaMallocHost(&ep->h_sched, sizeof(int32_t) * kSchedInts * world) != cudaSuccess ||
+      cudaMallocHost(&ep->h_sched, sizeof(int32_t) * kSchedInts * (world + 1)) != cudaSuccess ||
       cudaMallocHost(&ep->h_seq, sizeof(uint64_t)) != cudaSuccess ||
       cudaMallocHost(&ep->h_wait_idx, sizeof(int) * 2 * world) != cudaSuccess)
     return fail(B2_ERR_CUDA);
@@ -460,20 +461,24 @@ extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
 }
 
 // GEMM schedule of the segments that came from `src` (rows of the receive
-// buffer), or of the rank's own rows at their expert-sorted positions when
-// `self_rows` is set.  Returns the number of segments.
+// buffer), restricted to the source-relative rows [lo, hi); with `self_rows`
+// the rank's own rows are addressed at their expert-sorted positions
+// (self_base + row) instead.  Returns the number of segments.
 static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self_base,
-                      int32_t *h, int *mtiles) {
+                      int64_t lo, int64_t hi, int32_t *h, int *mtiles) {
   int32_t *hc = h, *ho = h + (kMaxGroups + 1), *hm = ho + (kMaxGroups + 1),
           *hg = hm + (kMaxGroups + 1);
   int n = 0, mt = 0;
   for (int g = 0; g < p.num_segments; ++g) {
     if (p.seg_source[g] != src) continue;
-    hc[n] = p.seg_cnt[g];
-    ho[n] = self_rows ? (int32_t)(self_base + p.seg_off[g] - p.recv_off[src]) : p.seg_off[g];
+    const int64_t a = std::max<int64_t>(p.seg_off[g] - p.recv_off[src], lo);
+    const int64_t b = std::min<int64_t>(p.seg_off[g] - p.recv_off[src] + p.seg_cnt[g], hi);
+    if (a >= b) continue;
+    hc[n] = (int32_t)(b - a);
+    ho[n] = (int32_t)(self_rows ? self_base + a : p.recv_off[src] + a);
     hg[n] = p.seg_expert[g];
     hm[n] = mt;
-    mt += (p.seg_cnt[g] + kBM - 1) / kBM;
+    mt += (int)((b - a + kBM - 1) / kBM);
     ++n;
   }
   hm[n] = mt;
@@ -511,16 +516,25 @@ extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
     B2_RETURN_IF(b2_ep_plan_compute(G, q, E, ep->mode, ep->h_cnt_all, &ep->plans[q]));
   const b2_ep_plan &p = ep->plans[r];
   if (p.recv_rows > ep->cap_rows) return B2_ERR_CAPACITY;
-  std::vector<int> nseg(G), mtiles(G);
-  for (int src = 0; src < G; ++src)
-    nseg[src] = fill_sched(p, src, src == r, p.send_off[r], ep->h_sched + (size_t)src * kSchedInts,
-                           &mtiles[src]);
+  // schedule slots: one per source; the rank's own rows are split in two
+  // (slot r before the remote steps, slot G after them) so that the return of
+  // the last remote step overlaps the second half
+  const int64_t self_rows = p.recv_cnt[r];
+  const int64_t self_b = G > 1 ? std::min<int64_t>(self_rows / 2, p.recv_cnt[(r + 1) % G]) : 0;
+  std::vector<int> nseg(G + 1), mtiles(G + 1);
+  for (int src = 0; src < G; ++src) {
+    const int64_t hi = src == r ? self_rows - self_b : INT64_MAX;
+    nseg[src] = fill_sched(p, src, src == r, p.send_off[r], 0, hi,
+                           ep->h_sched + (size_t)src * kSchedInts, &mtiles[src]);
+  }
+  nseg[G] = fill_sched(p, r, true, p.send_off[r], self_rows - self_b, self_rows,
+                       ep->h_sched + (size_t)G * kSchedInts, &mtiles[G]);
   int nwait_ret = 0;
   for (int d = 0; d < G; ++d)
     if (d != r && p.send_cnt[d] > 0) ep->h_wait_idx[G + nwait_ret++] = kFlagReturn * G + d;
   ep->seq += 1;
   *ep->h_seq = ep->seq;
-  B2_CUDA(cudaMemcpyAsync(ep->d_sched, ep->h_sched, sizeof(int32_t) * kSchedInts * G,
+  B2_CUDA(cudaMemcpyAsync(ep->d_sched, ep->h_sched, sizeof(int32_t) * kSchedInts * (G + 1),
                           cudaMemcpyHostToDevice, s));
   B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
   for (int src = 0; src < G; ++src) ep->h_wait_idx[src] = kFlagDispatch * G + src;
@@ -553,7 +567,7 @@ extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
     B2_CUDA(cudaMemcpyAsync(ep->peer_flags[to] + kFlagDispatch * G + r, ep->d_seq,
                             sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_d));
   }
-  // 4. own rows first, in place (sorted_x -> inter -> sout), while rows travel
+  // 4. first part of the own rows, in place (sorted_x -> inter -> sout), while rows travel
   if (nseg[r] > 0)
     B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(r), s,
                                 false));
@@ -577,6 +591,10 @@ extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
     B2_CUDA(cudaMemcpyAsync(ep->peer_flags[from] + kFlagReturn * G + r, ep->d_seq,
                             sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_r));
   }
+  // second part of the own rows while the last results travel back
+  if (nseg[G] > 0)
+    B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(G), s,
+                                false));
   prof_mark(m, s);  // expert GEMMs done; waiting for returns
   if (nwait_ret > 0) {
     wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(

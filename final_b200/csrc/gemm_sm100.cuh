@@ -186,6 +186,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(smem_u32(tmem_holder), kTmemCols);
     tmem_relinquish();
   }
+  // everything above overlaps the previous kernel's tail; the schedule and
+  // the A operand are that kernel's output
+  pdl_wait();
+  pdl_trigger();
   if (g.num_groups > 0) {
     for (int i = threadIdx.x; i <= g.num_groups; i += blockDim.x) {
       s_mt[i] = g.mtile_offsets[i];

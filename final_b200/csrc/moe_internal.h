@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <utility>
 #include <cstdio>
 #include <vector>
 
@@ -58,6 +59,27 @@ inline bool dev_info(DevInfo *d) {
   return true;
 }
 
+// Launch with programmatic stream serialization: the kernel may begin while
+// its predecessor in the stream drains; every kernel of this library calls
+// pdl_wait() before it reads anything a predecessor produced.
+template <typename... KArgs, typename... Args>
+b2_status launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
 template <int EPI, bool TF32, typename TOut>
 b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
                       int grid, cudaStream_t s) {
@@ -66,9 +88,7 @@ b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
   // per-device attribute; cheap enough to set on every launch
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   if (grid <= 0) return B2_OK;
-  kern<<<grid, kGemmThreads, smem, s>>>(ta, tb, args);
-  B2_LAUNCHED();
-  return B2_OK;
+  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, s, ta, tb, args);
 }
 
 // Row segments the two grouped GEMMs run over: group g covers rows

@@ -70,6 +70,8 @@ static __global__ void __launch_bounds__(kRouteThreads)
   const int t0 = blockIdx.x * kRouteTB;
   const int NC = H / kRouteKC;
   hist[lane] = 0;
+  pdl_wait();
+  pdl_trigger();
 
   // chunk kc -> stage st: 8 x 16 B of x and 8 x 16 B of the gate per lane;
   // rows past T are zero-filled (src-size 0)
@@ -231,6 +233,8 @@ static __global__ void __launch_bounds__(1024)
   __shared__ int ebase[32];
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
+  pdl_wait();
+  pdl_trigger();
   const int per = (nb + 31) / 32;
   const int b0 = w * per, b1 = min(nb, b0 + per);
   int s = 0;
@@ -296,6 +300,8 @@ __global__ void __launch_bounds__(256)
   const int lane = p & 31, w = p >> 5;
   const int t = blockIdx.x * kRouteTB + p / K;
   for (int i = p; i < 8 * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
   int e = -1;
   if (p < npairs && t < T) {
@@ -377,6 +383,7 @@ __global__ void __launch_bounds__(256)
   const int t = blockIdx.x;
   __shared__ int ss[kMaxTopK];
   __shared__ float sw[kMaxTopK];
+  pdl_wait();
   if (threadIdx.x < K) {
     ss[threadIdx.x] = token_slot[(size_t)t * K + threadIdx.x];
     sw[threadIdx.x] = topk_w[(size_t)t * K + threadIdx.x];

@@ -48,6 +48,16 @@ __device__ __forceinline__ bool elect_one_sync() {
   return pred != 0;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic-serialization attribute may start
+// while its predecessor in the stream is still running; pdl_wait() blocks until
+// that predecessor has completed and its memory is visible (a no-op for a
+// normal launch).  pdl_trigger() lets the successor start launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
