@@ -17,7 +17,7 @@ B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
 # Every symbol include/b2moe.h declares (checked by tests/test_abi.py).
 EXPORTED = (
     "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
-    "b2_moe_get_status", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
+    "b2_moe_get_status", "b2_moe_tile_rows", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
     "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
@@ -103,6 +103,7 @@ def load(path: Path | None = None):
     lib.b2_ep_layer.restype = vp
     lib.b2_ep_destroy.argtypes = [vp]
     lib.b2_kernel_launch_count.restype = C.c_uint64
+    lib.b2_moe_tile_rows.restype = i
     lib.b2_status_string.argtypes = [i]
     lib.b2_status_string.restype = C.c_char_p
     lib.b2_version.restype = C.c_char_p

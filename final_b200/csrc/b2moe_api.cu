@@ -208,7 +208,9 @@ b2_status moe_create_impl(const b2_moe_desc *desc, int n_wexp, const float *cons
   if (!make_tmap(&m->tm_x, m->sorted_x, f, H, R, (uint64_t)H * es, kBM) ||
       !make_tmap(&m->tm_w13, m->w13, f, H, (uint64_t)Wm * 2 * Ip, (uint64_t)H * es, kBN) ||
       (m->inter && !make_tmap(&m->tm_inter, m->inter, f, Ip, R, (uint64_t)Ip * es, kBM)) ||
-      !make_tmap(&m->tm_w2, m->w2, f, Ip, (uint64_t)Wm * H, (uint64_t)Ip * es, kBN))
+      !make_tmap(&m->tm_w2, m->w2, f, Ip, (uint64_t)Wm * H, (uint64_t)Ip * es, kBN) ||
+      !make_tmap(&m->tm_w13_half, m->w13, f, H, (uint64_t)Wm * 2 * Ip, (uint64_t)H * es, kBN / 2) ||
+      !make_tmap(&m->tm_w2_half, m->w2, f, Ip, (uint64_t)Wm * H, (uint64_t)Ip * es, kBN / 2))
     return bail(B2_ERR_CUDA);
 #undef B2_TRY
   *out = m;
@@ -226,7 +228,7 @@ b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *
                           tr ? tr->logits : (float *)nullptr));
   prof_mark(m, s);
   B2_RETURN_IF(launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, s, (const int *)m->block_counts, nb,
-                          E, (int)kBM, m->counts, m->offsets, m->mtile, m->block_base));
+                          E, (int)kPairBM, m->counts, m->offsets, m->mtile, m->block_base));
   prof_mark(m, s);
   if (m->tf32)
     B2_RETURN_IF(launch_pdl(scatter_kernel<float>, dim3(nb), dim3(scatter_threads(K)), 0, s, x,
@@ -248,6 +250,7 @@ b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap 
                          bool stage_marks) {
   const int H = m->d.hidden, Ip = m->Ip;
   const bool f = m->tf32;
+  const int max_pairs = m->sms / 2;
   GemmArgs a1{};
   a1.counts = sc.counts;
   a1.offsets = sc.offsets;
@@ -261,12 +264,13 @@ b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap 
   a1.out = inter;
   a1.ldo = Ip;
   a1.status = m->status;
-  const int grid1 = (int)std::min<long long>(m->sms, sc.mtiles_upper_bound * a1.num_n_tiles);
+  const int pairs1 = (int)std::min<long long>(max_pairs, sc.mtiles_upper_bound * a1.num_n_tiles);
   if (stage_marks) prof_mark(m, s);
   if (f)
-    B2_RETURN_IF((launch_gemm<kEpiSwiGLU, true, float>(tm_a1, m->tm_w13, a1, grid1, s)));
+    B2_RETURN_IF((launch_gemm_pair<kEpiSwiGLU, true, float>(tm_a1, m->tm_w13_half, a1, pairs1, s)));
   else
-    B2_RETURN_IF((launch_gemm<kEpiSwiGLU, false, __nv_bfloat16>(tm_a1, m->tm_w13, a1, grid1, s)));
+    B2_RETURN_IF(
+        (launch_gemm_pair<kEpiSwiGLU, false, __nv_bfloat16>(tm_a1, m->tm_w13_half, a1, pairs1, s)));
 
   GemmArgs a2 = a1;
   a2.b_rows_per_group = H;
@@ -275,12 +279,13 @@ b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap 
   a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
   a2.out = out;
   a2.ldo = H;
-  const int grid2 = (int)std::min<long long>(m->sms, sc.mtiles_upper_bound * a2.num_n_tiles);
+  const int pairs2 = (int)std::min<long long>(max_pairs, sc.mtiles_upper_bound * a2.num_n_tiles);
   if (stage_marks) prof_mark(m, s);
   if (f)
-    B2_RETURN_IF((launch_gemm<kEpiStore, true, float>(tm_a2, m->tm_w2, a2, grid2, s)));
+    B2_RETURN_IF((launch_gemm_pair<kEpiStore, true, float>(tm_a2, m->tm_w2_half, a2, pairs2, s)));
   else
-    B2_RETURN_IF((launch_gemm<kEpiStore, false, __nv_bfloat16>(tm_a2, m->tm_w2, a2, grid2, s)));
+    B2_RETURN_IF(
+        (launch_gemm_pair<kEpiStore, false, __nv_bfloat16>(tm_a2, m->tm_w2_half, a2, pairs2, s)));
   return B2_OK;
 }
 
@@ -333,7 +338,7 @@ extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int 
   sc.mtile_offsets = m->mtile;
   sc.group_b = nullptr;
   sc.num_groups = E;
-  sc.mtiles_upper_bound = ((long long)T * K + kBM - 1) / kBM + E;  // <= 1 partial tile per expert
+  sc.mtiles_upper_bound = ((long long)T * K + kPairBM - 1) / kPairBM + E;  // <= 1 partial tile per expert
   B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, m->tm_inter, m->inter, m->sout, sc, s));
   B2_RETURN_IF(moe_combine_stage(m, y, T, s));
 
@@ -420,9 +425,18 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
   g.out = C;
   g.ldo = ldc;
   g.status = status;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  const long long pair_tiles = (long long)((M + kPairBM - 1) / kPairBM) * g.num_n_tiles;
+  if (pair_tiles >= di.sms / 2) {
+    // enough 256x256 tiles to keep every CTA pair busy: the CTA-pair kernel
+    CUtensorMap tbh;
+    if (!make_tmap(&tbh, B, f, K, N, (uint64_t)K * es, kBN / 2)) return B2_ERR_INVALID;
+    const int pairs = (int)std::min<long long>(di.sms / 2, pair_tiles);
+    if (f) return launch_gemm_pair<kEpiStore, true, float>(ta, tbh, g, pairs, s);
+    return launch_gemm_pair<kEpiStore, false, float>(ta, tbh, g, pairs, s);
+  }
   const long long tiles = (long long)((M + kBM - 1) / kBM) * g.num_n_tiles;
   const int grid = (int)std::min<long long>(di.sms, tiles);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   if (f) return launch_gemm<kEpiStore, true, float>(ta, tb, g, grid, s);
   return launch_gemm<kEpiStore, false, float>(ta, tb, g, grid, s);
 }
@@ -441,6 +455,8 @@ extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n
 }
 
 extern "C" uint64_t b2_kernel_launch_count(void) { return launch_counter().load(); }
+
+extern "C" int b2_moe_tile_rows(void) { return kPairBM; }
 
 extern "C" const char *b2_status_string(b2_status s) {
   switch (s) {

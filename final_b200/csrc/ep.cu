@@ -478,7 +478,7 @@ static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self
     ho[n] = (int32_t)(self_rows ? self_base + a : p.recv_off[src] + a);
     hg[n] = p.seg_expert[g];
     hm[n] = mt;
-    mt += (int)((b - a + kBM - 1) / kBM);
+    mt += (int)((b - a + kPairBM - 1) / kPairBM);
     ++n;
   }
   hm[n] = mt;

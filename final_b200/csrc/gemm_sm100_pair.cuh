@@ -1,0 +1,284 @@
+// gemm_sm100_pair.cuh -- the tcgen05 GEMM of gemm_sm100.cuh run by CTA pairs
+// (cta_group::2): each pair of CTAs of a 2-CTA cluster computes a 256 x 256
+// output tile.
+//
+//   CTA c of the pair loads A rows [m0 + 128c, +128) and B rows [n0 + 128c,
+//   +128) of each 128-byte k-block into its own shared memory (a 6-stage ring
+//   of 32 KB stages); the pair leader (c = 0) issues M=256 x N=256 UMMAs that
+//   read both CTAs' shared memory and accumulate into both CTAs' TMEM (each CTA
+//   holds its 128 rows x 256 columns); every CTA runs the epilogue of its own
+//   rows.  Per CTA and k-block that is 32 KB of operand traffic instead of the
+//   48 KB of a single-CTA 128 x 256 tile.
+//
+// Synchronisation (all waits bounded as in sm100_ptx.cuh):
+//   full[s]    leader's barrier; both producers arrive, both CTAs' TMA bytes
+//              complete on it (cta_group::2 loads, no multicast);
+//   empty[s]   one per CTA; the leader commits its MMAs to both;
+//   tfull[a]   one per CTA; the leader commits the last k-block's MMAs to both;
+//   tempty[a]  leader's barrier; one arrival per epilogue warp of both CTAs.
+// The grouped schedule's m-tiles are 256 rows (mtile_offsets in 256-row units).
+#pragma once
+#include "gemm_sm100.cuh"
+
+namespace b2 {
+
+constexpr int kPairBM = 256;  // rows per CTA-pair tile (128 per CTA)
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = 128 * kBKBytes;  // 16 KB
+constexpr int kPairBBytes = 128 * kBKBytes;  // 16 KB: half of the 256-wide B tile
+
+constexpr size_t gemm_pair_smem_bytes() {
+  return 1024 + (size_t)kPairStages * (kPairABytes + kPairBBytes) + 512 + 4 * (kMaxGroups + 1) * 4;
+}
+
+__device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g, const int *s_mt,
+                                                     const int *s_off, const int *s_cnt,
+                                                     const int *s_grp, int out_tile_cols,
+                                                     int crank) {
+  TileInfo t;
+  const int NT = g.num_n_tiles;
+  if (g.num_groups > 0) {
+    const int gm = tile / NT;
+    const int n = tile - gm * NT;
+    int lo = 0, hi = g.num_groups;  // s_mt[lo] <= gm < s_mt[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_mt[mid] <= gm) lo = mid; else hi = mid;
+    }
+    const int m = gm - s_mt[lo];
+    t.a_row = s_off[lo] + m * kPairBM + 128 * crank;
+    t.rows_valid = min(128, s_cnt[lo] - m * kPairBM - 128 * crank);
+    t.b_row = s_grp[lo] * g.b_rows_per_group + n * kBN + 128 * crank;
+    t.n_tile = n;
+  } else {
+    const int MT = (g.M + kPairBM - 1) / kPairBM;
+    const int band = g.group_m * NT;
+    const int b = tile / band;
+    const int m0 = b * g.group_m;
+    const int gh = min(g.group_m, MT - m0);
+    const int idx = tile - b * band;
+    const int n = idx / gh;
+    const int m = m0 + (idx - n * gh);
+    t.a_row = m * kPairBM + 128 * crank;
+    t.rows_valid = min(128, g.M - t.a_row);
+    t.b_row = n * kBN + 128 * crank;
+    t.n_tile = n;
+  }
+  t.cols_valid = min(out_tile_cols, g.N - t.n_tile * out_tile_cols);
+  return t;
+}
+
+template <int EPI, bool TF32, typename TOut>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + kPairStages * kPairABytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + kPairStages * kPairBBytes);
+  // bars[0..S) full, [S..2S) empty, 2S..2S+1 tmem_full, 2S+2..2S+3 tmem_empty, 2S+4 drain
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kPairStages + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  int *s_mt = reinterpret_cast<int *>(bars) + 128;  // 512 B past the barrier block
+  int *s_off = s_mt + (kMaxGroups + 1);
+  int *s_cnt = s_off + (kMaxGroups + 1);
+  int *s_grp = s_cnt + (kMaxGroups + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[kPairStages + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * kPairStages + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * kPairStages + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[2 * kPairStages + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(full_bar(s), 2);   // both producers of the pair arrive (leader's copy is used)
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps x 2 CTAs (leader's copy is used)
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (g.num_groups > 0) {
+    for (int i = threadIdx.x; i <= g.num_groups; i += blockDim.x) {
+      s_mt[i] = g.mtile_offsets[i];
+      if (i < g.num_groups) {
+        s_off[i] = g.offsets[i];
+        s_cnt[i] = g.counts[i];
+        s_grp[i] = g.group_b ? g.group_b[i] : i;
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int NT = g.num_n_tiles;
+  const int total_tiles = g.num_groups > 0
+                              ? s_mt[g.num_groups] * NT
+                              : ((g.M + kPairBM - 1) / kPairBM) * NT;
+  constexpr int out_tile_cols = (EPI == kEpiSwiGLU) ? kBN / 2 : kBN;
+  const int KB = g.num_k_blocks;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer (both CTAs)
+      const uint64_t pol = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = pair; tile < total_tiles; tile += npairs) {
+        const TileInfo t =
+            decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols, (int)crank);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, g.status,
+                         kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lead_full = mapa_shared(full_bar(stage), 0);
+          if (leader)
+            mbar_arrive_expect_tx(full_bar(stage), 2 * (kPairABytes + kPairBBytes));
+          else
+            mbar_arrive_cluster(lead_full);
+          const int kc = kb * (TF32 ? 32 : 64);
+          tma_load_2d_pair(smem_u32(sA + stage * kPairABytes), &tmA, lead_full, kc, t.a_row, pol);
+          tma_load_2d_pair(smem_u32(sB + stage * kPairBBytes), &tmB, lead_full, kc, t.b_row, pol);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------ UMMA issuer (pair leader)
+      constexpr uint32_t idesc = make_idesc(TF32 ? 2u : 1u, 2 * 128, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_par = 0;
+      bool issued_any = false;
+      for (int tile = pair; tile < total_tiles; tile += npairs) {
+        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1, abort_flag, g.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, g.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a0 = make_sw128_desc(smem_u32(sA + stage * kPairABytes));
+          const uint64_t b0 = make_sw128_desc(smem_u32(sB + stage * kPairBBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (TF32)
+              umma_tf32_pair(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0);
+            else
+              umma_f16_pair(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0);
+          }
+          issued_any = true;
+          umma_commit_pair(empty_bar(stage));
+          umma_commit_pair(mapa_shared(empty_bar(stage), 1));
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc));
+        umma_commit_pair(mapa_shared(tfull_bar(acc), 1));
+        acc ^= 1;
+        if (acc == 0) acc_par ^= 1;
+      }
+      if (issued_any) {
+        umma_commit_pair(drain_bar);
+        mbar_drain(drain_bar, 0, g.status);
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool vec_ok = (g.ldo * (long long)sizeof(TOut)) % 16 == 0;
+    int acc = 0;
+    uint32_t acc_par = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs) {
+      const TileInfo t =
+          decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols, (int)crank);
+      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+      const bool row_ok = row < t.rows_valid;
+      TOut *out = reinterpret_cast<TOut *>(g.out) + (long long)(t.a_row + row) * g.ldo +
+                  (long long)t.n_tile * out_tile_cols;
+      if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t gr[32], ur[32];
+          tmem_ld32(tbase + c * 32, gr);
+          tmem_ld32(tbase + 128 + c * 32, ur);
+          tmem_ld_wait();
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gv = __uint_as_float(gr[i]);
+            h[i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(ur[i]);
+          }
+          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) h[i] = __uint_as_float(r[i]);
+          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+      acc ^= 1;
+      if (acc == 0) acc_par ^= 1;
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into this CTA's TMEM are drained
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b2

@@ -13,6 +13,7 @@
 
 #include "../../include/b2moe.h"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_pair.cuh"
 #include "host_tmap.h"
 #include "moe_kernels.cuh"
 
@@ -91,13 +92,41 @@ b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
   return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, s, ta, tb, args);
 }
 
+// The same GEMM run by CTA pairs (2-CTA clusters, cta_group::2 UMMA): `pairs`
+// clusters of two CTAs.  The grouped schedule's m-tiles are kPairBM rows.
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
+                           int pairs, cudaStream_t s) {
+  auto kern = gemm_pair_kernel<EPI, TF32, TOut>;
+  const size_t smem = gemm_pair_smem_bytes();
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (pairs <= 0) return B2_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
 // Row segments the two grouped GEMMs run over: group g covers rows
 // [offsets[g], offsets[g] + counts[g]) of A and C and multiplies them with
 // expert block group_b[g] (or g when group_b is null) of the weights.
 struct GemmSched {
   const int *counts = nullptr;
   const int *offsets = nullptr;
-  const int *mtile_offsets = nullptr;  // exclusive prefix of ceil(count/128), [groups+1]
+  const int *mtile_offsets = nullptr;  // exclusive prefix of ceil(count/kPairBM), [groups+1]
   const int *group_b = nullptr;
   int num_groups = 0;
   long long mtiles_upper_bound = 0;    // sizes the persistent grid
@@ -127,6 +156,7 @@ struct b2_moe {
   void *sorted_x = nullptr, *inter = nullptr, *sout = nullptr;
   int *status = nullptr;
   CUtensorMap tm_x, tm_w13, tm_inter, tm_w2;
+  CUtensorMap tm_w13_half, tm_w2_half;  // B maps with 128-row boxes for the CTA-pair GEMM
   std::vector<void *> allocs;
   // stage profiling
   bool profile = false;

@@ -133,6 +133,10 @@ b2_status b2_moe_profile_enable(b2_moe *moe, int enable);
  * record. */
 b2_status b2_moe_profile_read(b2_moe *moe, float *stage_ms, int *forwards);
 
+/* Rows per m-tile of the expert GEMMs' schedule (the unit of
+ * b2_moe_trace.mtile_offsets). */
+int b2_moe_tile_rows(void);
+
 /* Bytes of device memory the object holds (weights + scratch). */
 size_t b2_moe_device_bytes(const b2_moe *moe);
 

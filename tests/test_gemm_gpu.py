@@ -23,6 +23,8 @@ SHAPES = [
     (64, 65536, 2048),    # LM head, batch rows only
     (1, 512, 2048),       # single row
     (1000, 520, 1032),    # K not a multiple of the 64-wide k-block
+    (4096, 3072, 2048),   # enough 256x256 tiles for the CTA-pair kernel
+    (2000, 4096, 1024),   # CTA-pair kernel with a ragged last row tile
 ]
 
 

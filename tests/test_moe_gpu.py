@@ -2,7 +2,7 @@
 
 Bit-exact (integer / index / routing work, per the reference's semantics):
   router logits, top-k expert ids (rank order), top-k weights, expert counts,
-  offsets, 128-row tile prefix, token -> slot map, slot -> token map and slot
+  offsets, m-tile prefix (b2_moe_tile_rows rows), token -> slot map, slot -> token map and slot
   weights (canonical token-major order).
 Within tolerance (max |y - y_ref| / max |y_ref|, y_ref = fp32 oracle):
   bf16 expert GEMMs, fp32 accumulate: 1e-2    tf32 expert GEMMs: 5e-3
@@ -33,7 +33,10 @@ def _rel(a, b):
 
 
 def _check_routing(got, ref):
+    import oracle
+    from final_b200 import load
     g = {k: v.cpu().numpy() for k, v in got.items()}
+    _, ref["mtile_offsets"] = oracle.scan(ref["counts"], load().b2_moe_tile_rows())
     assert np.array_equal(g["logits"].view(np.uint32), ref["logits"].view(np.uint32)), "logits"
     assert np.array_equal(g["topk_idx"], ref["topk_idx"]), "topk_idx"
     assert np.array_equal(g["topk_w"].view(np.uint32), ref["topk_w"].view(np.uint32)), "topk_w"
