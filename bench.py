@@ -9,9 +9,11 @@ x[:, :32] = ln p_e + Gumbel noise; the router GEMM still runs over all 2048
 columns).  One step = one full layer forward (route, scan, scatter, W1/W3
 SwiGLU grouped GEMM, W2 grouped GEMM, combine) on inputs resident in HBM.
 
-With --gpus N (launched under torchrun) every rank runs the same layer on its
-own 16384 tokens (independent replicas; expert-parallel exchange is not part
-of this line), value = all ranks' tokens / max-over-ranks device time.
+With --gpus N (launched under torchrun) the layer runs expert-parallel: every
+rank routes its own 16384 tokens, rows travel to the rank that computes their
+expert segment and back (copy-engine writes into CUDA-IPC-mapped peer buffers,
+NCCL for the per-forward count all-gather), value = all ranks' tokens /
+max-over-ranks device time (weak scaling).
 
 --impl reference times the reference's own implementation of the path on the
 box's host cores (the C restatement in oracle/, since the reference ships no
@@ -69,19 +71,56 @@ def peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock, power and clock-event reasons sampled while the timed region
+    runs: NVML polled every 5 ms from a host thread (the main thread sits in
+    cudaDeviceSynchronize meanwhile), so even a timed region of a few tens of
+    ms gets several samples; nvidia-smi at 200 ms if NVML is unavailable.
+    Read-only queries: no clock or power setting is touched."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4),
+               ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, smi_index):
+    def __init__(self, smi_index, period_s=0.005):
         self.idx = smi_index
+        self.period = period_s
         self.proc = None
         self.path = None
+        self.thread = None
+        self.rows = []
+        self.nvml = None
 
     def start(self):
         if self.idx is None:
+            return
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.stop_flag = threading.Event()
+            nv = self.nvml
+
+            def poll():
+                while True:
+                    try:
+                        self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                          nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                          int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                    except Exception:
+                        pass
+                    if self.stop_flag.wait(self.period):
+                        break
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
             return
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
@@ -94,6 +133,17 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join()
+            self.nvml.nvmlShutdown()
+            if not self.rows:
+                return None
+            sm = sorted(r[0] for r in self.rows)
+            reasons = sorted({n for n, bit in self.REASONS for r in self.rows if r[2] & bit})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz,
+                    "sm_mhz_min": sm[0], "power_w_max": max(r[1] for r in self.rows),
+                    "reasons": reasons, "samples": len(self.rows), "sampler": "nvml 5 ms"}
         if self.proc is None:
             return None
         time.sleep(0.25)
@@ -121,7 +171,7 @@ class ClockSampler:
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
                 if any(r[3].replace(".", "").isdigit() for r in rows) else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows), "sampler": "nvidia-smi 200 ms"}
 
 
 def smi_index_for(dev_index: int):
@@ -237,10 +287,10 @@ def run_ours(args, rank, world, dev):
         fwd(x, y)
     ev1.record(stream)
     torch.cuda.synchronize()
+    clocks = sampler.stop()
     n1 = launch_count()
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
     # the same K steps again with CUDA events between the stages (kept out of the
     # timed region above: an event between two kernels stops the second one from
@@ -351,13 +401,14 @@ def run_ours(args, rank, world, dev):
                        counts_probe if world > 1 else [max(counts_probe), min(counts_probe)],
                    "weights": f"{args.dtype} packed from fp32 N(0,0.02)",
                    "l2": "inputs larger than L2: x 134 MB fp32, expert weights 705 MB bf16",
-                   "parallelism": (f"expert-parallel ep{world} ({args.ep_mode}), NCCL dispatch/combine"
+                   "parallelism": (f"expert-parallel ep{world} ({args.ep_mode}), copy-engine peer "
+                                   "dispatch/combine, NCCL count all-gather"
                                    if world > 1 else "single")},
         "layer_tflops": flop * args.steps * world / (ms / 1e3) / 1e12 / world,
         "grouped_gemm_tflops": gemm_flop / ((w13_ms + w2_ms) / 1e3) / 1e12,
         "frac_of_bf16_peak_layer": flop / (ms / args.steps / 1e3) / 1e12 / pk["bf16"],
         "stages_ms_per_step": {k: v / max(nfw, 1) for k, v in stage_ms.items()},
-        "roofline": {"kernel": "gemm_sm100_kernel<SwiGLU,bf16> (W1||W3 grouped GEMM)",
+        "roofline": {"kernel": "gemm_pair_kernel<SwiGLU,bf16> (W1||W3 grouped GEMM, CTA pairs)",
                      "bound": "tensor", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -380,13 +431,38 @@ DENSE_M = (512, 4096, 16384)
 DENSE_N = (2048, 3072, 65536)
 
 
-def dense_sweep(dev, K=2048, reps=5):
+def dense_sweep(dev, K=2048, reps=10):
     """C[M,N] = A[M,2048] . B[N,2048]^T on the tcgen05 core,
-    bf16 operands and fp32 operands (TF32 math), fp32 output; TFLOP/s per shape."""
+    bf16 operands and fp32 operands (TF32 math), fp32 output; TFLOP/s per shape.
+
+    Device time per GEMM: `reps` b2_gemm_nt calls are captured once into a CUDA
+    graph and the replay is timed with CUDA events, so the host-side cost of a
+    call (ctypes, tensor-map encoding) does not hide the kernel time of the
+    small shapes.  cublas_bf16_tflops is torch.mm (cuBLAS, bf16 in and out) on
+    the same bf16 operands, timed the same way, for comparison only."""
     import torch
     from final_b200 import gemm_nt, to_bf16
     res = []
     g = torch.Generator(device=dev).manual_seed(2)
+
+    def graph_ms(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / reps
+
     for M in DENSE_M:
         for N in DENSE_N:
             A = torch.randn(M, K, device=dev, generator=g)
@@ -394,18 +470,13 @@ def dense_sweep(dev, K=2048, reps=5):
             C = torch.empty(M, N, device=dev)
             Ab, Bb = to_bf16(A), to_bf16(B)
             row = {"M": M, "N": N, "K": K}
+            flop = 2.0 * M * N * K
             for name, a, b in (("bf16", Ab, Bb), ("tf32", A, B)):
-                for _ in range(2):
-                    gemm_nt(a, b, out=C, dtype=name)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                for _ in range(reps):
-                    gemm_nt(a, b, out=C, dtype=name)
-                e1.record()
-                torch.cuda.synchronize()
-                ms = e0.elapsed_time(e1) / reps
-                row[f"{name}_tflops"] = 2.0 * M * N * K / (ms / 1e3) / 1e12
+                ms = graph_ms(lambda: gemm_nt(a, b, out=C, dtype=name))
+                row[f"{name}_tflops"] = flop / (ms / 1e3) / 1e12
                 row[f"{name}_ms"] = ms
+            ms = graph_ms(lambda: torch.mm(Ab, Bb.t()))
+            row["cublas_bf16_tflops"] = flop / (ms / 1e3) / 1e12
             res.append(row)
             del A, B, C, Ab, Bb
     torch.cuda.empty_cache()

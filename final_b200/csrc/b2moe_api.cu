@@ -435,10 +435,31 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
     if (f) return launch_gemm_pair<kEpiStore, true, float>(ta, tbh, g, pairs, s);
     return launch_gemm_pair<kEpiStore, false, float>(ta, tbh, g, pairs, s);
   }
-  const long long tiles = (long long)((M + kBM - 1) / kBM) * g.num_n_tiles;
-  const int grid = (int)std::min<long long>(di.sms, tiles);
-  if (f) return launch_gemm<kEpiStore, true, float>(ta, tb, g, grid, s);
-  return launch_gemm<kEpiStore, false, float>(ta, tb, g, grid, s);
+  // Too few 256x256 tiles: one CTA per 128 x BN tile, BN the widest of 256 /
+  // 128 / 64 that still gives every SM a tile (narrower tiles move more
+  // operand bytes per FLOP, so they only pay when SMs would otherwise idle).
+  const long long mt = (M + kBM - 1) / kBM;
+  int bn = 64;
+  for (int c : {256, 128}) {
+    if (mt * ((N + c - 1) / c) >= di.sms) {
+      bn = c;
+      break;
+    }
+  }
+  g.num_n_tiles = (N + bn - 1) / bn;
+  if (bn != kBN && !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, bn)) return B2_ERR_INVALID;
+  const int grid = (int)std::min<long long>(di.sms, mt * g.num_n_tiles);
+  switch (bn) {
+    case 256:
+      return f ? launch_gemm<kEpiStore, true, float, 256>(ta, tb, g, grid, s)
+               : launch_gemm<kEpiStore, false, float, 256>(ta, tb, g, grid, s);
+    case 128:
+      return f ? launch_gemm<kEpiStore, true, float, 128>(ta, tb, g, grid, s)
+               : launch_gemm<kEpiStore, false, float, 128>(ta, tb, g, grid, s);
+    default:
+      return f ? launch_gemm<kEpiStore, true, float, 64>(ta, tb, g, grid, s)
+               : launch_gemm<kEpiStore, false, float, 64>(ta, tb, g, grid, s);
+  }
 }
 
 extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,

@@ -28,7 +28,8 @@ constexpr int kPairABytes = 128 * kBKBytes;  // 16 KB
 constexpr int kPairBBytes = 128 * kBKBytes;  // 16 KB: half of the 256-wide B tile
 
 constexpr size_t gemm_pair_smem_bytes() {
-  return 1024 + (size_t)kPairStages * (kPairABytes + kPairBBytes) + 512 + 4 * (kMaxGroups + 1) * 4;
+  return 1024 + (size_t)kPairStages * (kPairABytes + kPairBBytes) + kEpiStageBytes + 512 +
+         4 * (kMaxGroups + 1) * 4;
 }
 
 __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g, const int *s_mt,
@@ -77,7 +78,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sB = smem + kPairStages * kPairABytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + kPairStages * kPairBBytes);
+  uint8_t *sEpi = sB + kPairStages * kPairBBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + kEpiStageBytes);
   // bars[0..S) full, [S..2S) empty, 2S..2S+1 tmem_full, 2S+2..2S+3 tmem_empty, 2S+4 drain
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kPairStages + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
@@ -147,6 +149,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint64_t pol = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t issued = 0, last_par = 0;
       for (int tile = pair; tile < total_tiles; tile += npairs) {
         const TileInfo t =
             decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols, (int)crank);
@@ -165,6 +168,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int kc = kb * (TF32 ? 32 : 64);
           tma_load_2d_pair(smem_u32(sA + stage * kPairABytes), &tmA, lead_full, kc, t.a_row, pol);
           tma_load_2d_pair(smem_u32(sB + stage * kPairBBytes), &tmB, lead_full, kc, t.b_row, pol);
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
@@ -172,6 +177,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (!ok) break;
       }
+      // Both CTAs' copies complete on the leader's full barriers: the leader
+      // waits (bounded) for the last phase of every stage it filled before
+      // the pair leaves; the peer stays resident meanwhile in the final
+      // cluster barrier.  Without an abort this returns at once (the MMA
+      // warp has consumed every stage).
+      if (leader)
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued >> s & 1) mbar_drain(full_bar(s), (last_par >> s) & 1, g.status);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // -------------------------------------------------- epilogue (both CTAs)
     const int q = warp & 3;
-    const int row = q * 32 + lane;
+    uint8_t *stage = sEpi + q * kEpiWarpBytes;
     const bool vec_ok = (g.ldo * (long long)sizeof(TOut)) % 16 == 0;
     int acc = 0;
     uint32_t acc_par = 0;
@@ -235,8 +248,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
-      const bool row_ok = row < t.rows_valid;
-      TOut *out = reinterpret_cast<TOut *>(g.out) + (long long)(t.a_row + row) * g.ldo +
+      const int rows_valid = t.rows_valid - q * 32;  // of this warp's 32 rows
+      TOut *out = reinterpret_cast<TOut *>(g.out) + (long long)(t.a_row + q * 32) * g.ldo +
                   (long long)t.n_tile * out_tile_cols;
       if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll 1
@@ -251,7 +264,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const float gv = __uint_as_float(gr[i]);
             h[i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(ur[i]);
           }
-          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+          store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
+                      lane);
         }
       } else {
 #pragma unroll 1
@@ -262,7 +276,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float h[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) h[i] = __uint_as_float(r[i]);
-          if (row_ok) store_cols(out + c * 32, h, t.cols_valid - c * 32, vec_ok);
+          store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
+                      lane);
         }
       }
       tc_fence_before();

@@ -81,13 +81,27 @@ b2_status launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   return B2_OK;
 }
 
-template <int EPI, bool TF32, typename TOut>
+// Raise a kernel's dynamic shared-memory limit once per device (the
+// attribute is per device and per kernel; setting it costs a driver call).
+// `done` belongs to the one kernel `kern`: one bit per device ordinal < 64.
+template <typename Kern>
+b2_status ensure_smem_limit(Kern kern, size_t smem, std::atomic<uint64_t> &done) {
+  int dev = 0;
+  B2_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? 1ull << dev : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return B2_OK;
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return B2_OK;
+}
+
+template <int EPI, bool TF32, typename TOut, int BN = kBN>
 b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
                       int grid, cudaStream_t s) {
-  auto kern = gemm_sm100_kernel<EPI, TF32, TOut>;
-  const size_t smem = gemm_smem_bytes();
-  // per-device attribute; cheap enough to set on every launch
-  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  auto kern = gemm_sm100_kernel<EPI, TF32, TOut, BN>;
+  const size_t smem = gemm_smem_bytes(BN);
+  static std::atomic<uint64_t> attr_done{0};  // per template instance = per kernel
+  B2_RETURN_IF(ensure_smem_limit(kern, smem, attr_done));
   if (grid <= 0) return B2_OK;
   return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, s, ta, tb, args);
 }
@@ -99,7 +113,8 @@ b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const G
                            int pairs, cudaStream_t s) {
   auto kern = gemm_pair_kernel<EPI, TF32, TOut>;
   const size_t smem = gemm_pair_smem_bytes();
-  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  static std::atomic<uint64_t> attr_done{0};  // per template instance = per kernel
+  B2_RETURN_IF(ensure_smem_limit(kern, smem, attr_done));
   if (pairs <= 0) return B2_OK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);

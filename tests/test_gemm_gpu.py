@@ -15,10 +15,14 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
+# On 148 SMs the shapes below reach every kernel configuration: CTA pairs
+# (256x256 tiles) and single CTAs with 256-, 128- and 64-column tiles.
 SHAPES = [
     (128, 256, 64),
-    (200, 300, 128),      # ragged M and N, one partial k-block
-    (512, 2048, 2048),    # out projection, M=512
+    (200, 300, 128),      # ragged M and N, one partial k-block (64-column tiles)
+    (512, 2048, 2048),    # out projection, M=512 (64-column tiles)
+    (1280, 2048, 2048),   # 128-column tiles
+    (300, 1000, 512),     # 64-column tiles, ragged last column tile
     (384, 3072, 2048),    # fused QKV width
     (64, 65536, 2048),    # LM head, batch rows only
     (1, 512, 2048),       # single row
