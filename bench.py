@@ -421,6 +421,7 @@ def run_ours(args, rank, world, dev):
         out["e2e"] = e2e
     if not args.no_dense and rank == 0:
         out["dense_gemm_sweep"] = dense_sweep(dev)
+        out["dense_mlp"] = mlp_bench(dev)
     if w_host is not None:
         out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
     return out
@@ -481,6 +482,41 @@ def dense_sweep(dev, K=2048, reps=10):
             del A, B, C, Ab, Bb
     torch.cuda.empty_cache()
     return res
+
+
+def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
+    """Dense SwiGLU MLP of the layers without experts (I = 7168) over T tokens
+    on the same GEMM core: tokens/s and TFLOP/s (6*T*H*I FLOP per forward)."""
+    import torch
+    from final_b200 import MLP
+    g = torch.Generator(device=dev).manual_seed(3)
+    w1 = torch.randn(Id, Hd, device=dev, generator=g) * 0.02
+    w3 = torch.randn(Id, Hd, device=dev, generator=g) * 0.02
+    w2 = torch.randn(Hd, Id, device=dev, generator=g) * 0.02
+    mlp = MLP(w1, w2, w3, max_tokens=T)
+    del w1, w2, w3
+    x = torch.randn(T, Hd, device=dev, generator=g)
+    y = torch.empty(T, Hd, device=dev)
+    out = {"tokens": T, "hidden": Hd, "inter": Id}
+    for name, n in (("prefill", T), ("decode_64", 64)):
+        for _ in range(3):
+            mlp.forward_gpu(x, y, 1, n, Hd)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            mlp.forward_gpu(x, y, 1, n, Hd)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        out[name] = {"tokens": n, "ms": ms, "tokens_per_s": n / (ms / 1e3),
+                     "tflops": 6.0 * n * Hd * Id / (ms / 1e3) / 1e12}
+    st = mlp.device_status()
+    mlp.close()
+    if st:
+        raise RuntimeError(f"MLP device status 0x{st:x}")
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------ CPU

@@ -14,7 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2moe.so"
 B2_OK, B2_ERR_INVALID, B2_ERR_CUDA, B2_ERR_CAPACITY, B2_ERR_DEVICE, B2_ERR_NO_DEVICE, B2_ERR_COMM = range(7)
 B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
 
-# Every symbol include/b2moe.h declares (checked by tests/test_abi.py).
+# Every symbol include/*.h declares (checked by tests/test_abi.py).
 EXPORTED = (
     "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
     "b2_moe_get_status", "b2_moe_tile_rows", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
@@ -22,6 +22,9 @@ EXPORTED = (
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
     "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy",
+    # include/b2mlp.h
+    "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_device_bytes",
+    "b2_mlp_destroy",
 )
 
 EP_MAX_WORLD = 64
@@ -40,6 +43,11 @@ class MoeDesc(C.Structure):
     _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("num_experts", C.c_int),
                 ("top_k", C.c_int), ("max_tokens", C.c_int), ("routed_scale", C.c_float),
                 ("use_bias", C.c_int), ("dtype", C.c_int)]
+
+
+class MlpDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("max_tokens", C.c_int),
+                ("dtype", C.c_int)]
 
 
 class MoeTrace(C.Structure):
@@ -102,6 +110,12 @@ def load(path: Path | None = None):
     lib.b2_ep_layer.argtypes = [vp]
     lib.b2_ep_layer.restype = vp
     lib.b2_ep_destroy.argtypes = [vp]
+    lib.b2_mlp_create.argtypes = [C.POINTER(MlpDesc), vp, vp, vp, i, vp, C.POINTER(vp)]
+    lib.b2_mlp_forward.argtypes = [vp, vp, vp, i, vp]
+    lib.b2_mlp_get_status.argtypes = [vp, vp, C.POINTER(i)]
+    lib.b2_mlp_device_bytes.argtypes = [vp]
+    lib.b2_mlp_device_bytes.restype = sz
+    lib.b2_mlp_destroy.argtypes = [vp]
     lib.b2_kernel_launch_count.restype = C.c_uint64
     lib.b2_moe_tile_rows.restype = i
     lib.b2_status_string.argtypes = [i]
@@ -111,7 +125,8 @@ def load(path: Path | None = None):
                  "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
                  "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc",
                  "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
-                 "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy"):
+                 "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy",
+                 "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_destroy"):
         getattr(lib, name).restype = i
     _lib = lib
     return lib

@@ -411,55 +411,22 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
   DevInfo di;
   if (!dev_info(&di)) return B2_ERR_NO_DEVICE;
   const size_t es = f ? 4 : 2;
+  const DensePlan plan = plan_dense(M, N, di.sms, false);
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, A, f, K, M, (uint64_t)K * es, kBM) ||
-      !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, kBN))
+      !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, plan.b_box_rows))
     return B2_ERR_INVALID;
   GemmArgs g{};
-  g.num_groups = 0;
   g.M = M;
   g.N = N;
-  g.num_n_tiles = (N + kBN - 1) / kBN;
   g.num_k_blocks = (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes);
   g.group_m = 16;
   g.out = C;
   g.ldo = ldc;
   g.status = status;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
-  const long long pair_tiles = (long long)((M + kPairBM - 1) / kPairBM) * g.num_n_tiles;
-  if (pair_tiles >= di.sms / 2) {
-    // enough 256x256 tiles to keep every CTA pair busy: the CTA-pair kernel
-    CUtensorMap tbh;
-    if (!make_tmap(&tbh, B, f, K, N, (uint64_t)K * es, kBN / 2)) return B2_ERR_INVALID;
-    const int pairs = (int)std::min<long long>(di.sms / 2, pair_tiles);
-    if (f) return launch_gemm_pair<kEpiStore, true, float>(ta, tbh, g, pairs, s);
-    return launch_gemm_pair<kEpiStore, false, float>(ta, tbh, g, pairs, s);
-  }
-  // Too few 256x256 tiles: one CTA per 128 x BN tile, BN the widest of 256 /
-  // 128 / 64 that still gives every SM a tile (narrower tiles move more
-  // operand bytes per FLOP, so they only pay when SMs would otherwise idle).
-  const long long mt = (M + kBM - 1) / kBM;
-  int bn = 64;
-  for (int c : {256, 128}) {
-    if (mt * ((N + c - 1) / c) >= di.sms) {
-      bn = c;
-      break;
-    }
-  }
-  g.num_n_tiles = (N + bn - 1) / bn;
-  if (bn != kBN && !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, bn)) return B2_ERR_INVALID;
-  const int grid = (int)std::min<long long>(di.sms, mt * g.num_n_tiles);
-  switch (bn) {
-    case 256:
-      return f ? launch_gemm<kEpiStore, true, float, 256>(ta, tb, g, grid, s)
-               : launch_gemm<kEpiStore, false, float, 256>(ta, tb, g, grid, s);
-    case 128:
-      return f ? launch_gemm<kEpiStore, true, float, 128>(ta, tb, g, grid, s)
-               : launch_gemm<kEpiStore, false, float, 128>(ta, tb, g, grid, s);
-    default:
-      return f ? launch_gemm<kEpiStore, true, float, 64>(ta, tb, g, grid, s)
-               : launch_gemm<kEpiStore, false, float, 64>(ta, tb, g, grid, s);
-  }
+  if (f) return launch_dense<kEpiStore, true, float>(plan, ta, tb, g, di.sms, s);
+  return launch_dense<kEpiStore, false, float>(plan, ta, tb, g, di.sms, s);
 }
 
 extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,

@@ -135,6 +135,58 @@ b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const G
   return B2_OK;
 }
 
+// Kernel configuration of a dense (single-group) GEMM over M rows and
+// n_tiles 256-wide B tiles (for SwiGLU a 256-wide B tile gives 128 outputs).
+//   pair  CTA-pair kernel (256x256 tiles) when they keep every pair busy;
+//   bn    else the single-CTA kernel's tile width: the widest of 256 / 128 /
+//         64 that gives every SM a tile (SwiGLU always 256: its B tile holds
+//         128 gate and 128 up rows).
+struct DensePlan {
+  bool pair;
+  int bn;
+  int b_box_rows;  // rows of the B tensor map's box
+};
+
+inline DensePlan plan_dense(long long M, int N, int sms, bool swiglu) {
+  const long long nt256 = swiglu ? N / 128 : (N + kBN - 1) / kBN;
+  if (((M + kPairBM - 1) / kPairBM) * nt256 >= sms / 2) return {true, kBN, kBN / 2};
+  if (swiglu) return {false, kBN, kBN};
+  const long long mt = (M + kBM - 1) / kBM;
+  for (int c : {256, 128})
+    if (mt * ((N + c - 1) / c) >= sms) return {false, c, c};
+  return {false, 64, 64};
+}
+
+// Launches a dense GEMM planned by plan_dense.  g.M, g.N, g.num_k_blocks,
+// g.out, g.ldo and g.status are set by the caller; tb's box has
+// plan.b_box_rows rows.
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_dense(const DensePlan &plan, const CUtensorMap &ta, const CUtensorMap &tb,
+                       GemmArgs g, int sms, cudaStream_t s) {
+  g.num_groups = 0;
+  if (g.group_m <= 0) g.group_m = 16;
+  const long long mt_pair = (g.M + kPairBM - 1) / kPairBM, mt = (g.M + kBM - 1) / kBM;
+  if (EPI == kEpiSwiGLU) {
+    g.num_n_tiles = g.N / 128;
+  } else {
+    g.num_n_tiles = (g.N + plan.bn - 1) / plan.bn;
+  }
+  if (plan.pair) {
+    const int pairs = (int)std::min<long long>(sms / 2, mt_pair * g.num_n_tiles);
+    return launch_gemm_pair<EPI, TF32, TOut>(ta, tb, g, pairs, s);
+  }
+  const int grid = (int)std::min<long long>(sms, mt * g.num_n_tiles);
+  if constexpr (EPI == kEpiSwiGLU) {
+    return launch_gemm<EPI, TF32, TOut, 256>(ta, tb, g, grid, s);
+  } else {
+    switch (plan.bn) {
+      case 256: return launch_gemm<EPI, TF32, TOut, 256>(ta, tb, g, grid, s);
+      case 128: return launch_gemm<EPI, TF32, TOut, 128>(ta, tb, g, grid, s);
+      default: return launch_gemm<EPI, TF32, TOut, 64>(ta, tb, g, grid, s);
+    }
+  }
+}
+
 // Row segments the two grouped GEMMs run over: group g covers rows
 // [offsets[g], offsets[g] + counts[g]) of A and C and multiplies them with
 // expert block group_b[g] (or g when group_b is null) of the weights.

@@ -462,8 +462,13 @@ static __global__ void pack_gate_kernel(const float *__restrict__ gate, int E, i
   gateT[i] = e < E ? gate[(size_t)e * H + h] : 0.0f;
 }
 
+// fp32 -> bf16 (round to nearest even), 8 elements per thread and step.  May
+// be launched with programmatic stream serialization: reads `in` only after
+// the predecessor kernel has completed.
 static __global__ void f32_to_bf16_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out,
                                    size_t n) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const size_t stride = (size_t)gridDim.x * blockDim.x * 8;
   for (; i + 8 <= n; i += stride) {

@@ -176,6 +176,19 @@ def expert_ffn(x, sorted_token, offsets, counts, w1, w3, w2, want_inter=False):
     return (out, inter) if want_inter else out
 
 
+def dense_mlp(x, w1, w3, w2):
+    """Dense SwiGLU MLP of the layers without experts, MLP::forward_gpu
+    (src/layer.cu:1230-1269): gate = x.W1^T, up = x.W3^T (attn_matmul_tiled_kernel,
+    src/layer.cu:9-141), silu(gate) * up (moe_swiglu_kernel, :670-692), then
+    .W2^T.  Every row goes through the expert FFN restatement as one expert
+    holding all rows (the same arithmetic, row by row)."""
+    T = x.shape[0]
+    counts = np.array([T], dtype=np.int32)
+    offsets = np.zeros(1, dtype=np.int32)
+    order = np.arange(T, dtype=np.int32)
+    return expert_ffn(x, order, offsets, counts, w1[None], w3[None], w2[None])[:T]
+
+
 def combine(out, token_slot, w, H):
     T, K = token_slot.shape
     y = np.empty((T, H), dtype=np.float32)
