@@ -63,6 +63,34 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+CPPDIR = PKG / "cpp"
+LAYERS_LIB = LIBDIR / "libb2layers.so"
+LAYERS_RUN = LIBDIR / "b2_layers_run"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+
+
+def build_cpp(force: bool = False, verbose: bool = False) -> None:
+    """The C++ drop-in layer classes (cpp/b2_layers.*) as libb2layers.so over
+    libb2moe.so, and the b2_layers_run driver the parity tests use."""
+    deps = list(CPPDIR.glob("*")) + [LIB] + list((ROOT / "include").glob("*.h"))
+    if not force and not _needs_rebuild(LAYERS_LIB, deps) and not _needs_rebuild(LAYERS_RUN, deps):
+        return
+    inc = ["-I", str(CUDA_HOME / "include")]
+    rpath = ["-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{CUDA_HOME / 'lib64'}"]
+    cmds = [
+        ["g++", "-std=c++17", "-O2", "-Wall", "-fPIC", "-shared", *inc,
+         str(CPPDIR / "b2_layers.cpp"), "-o", str(LAYERS_LIB), "-L", str(LIBDIR), "-lb2moe",
+         *rpath],
+        ["g++", "-std=c++17", "-O2", "-Wall", *inc, str(CPPDIR / "b2_layers_run.cpp"),
+         "-o", str(LAYERS_RUN), "-L", str(LIBDIR), "-lb2layers", "-lb2moe",
+         "-L", str(CUDA_HOME / "lib64"), "-lcudart", *rpath],
+    ]
+    for cmd in cmds:
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Build the CPU oracle (and oracle/_ref when the reference tree exists)."""
     cmd = ["make", "-C", str(ROOT / "oracle")]
@@ -73,4 +101,5 @@ def build_oracle(verbose: bool = False) -> None:
 
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose=True)
+    build_cpp(force="--force" in sys.argv, verbose=True)
     build_oracle(verbose=True)

@@ -1,0 +1,86 @@
+"""The C++ drop-in layer classes (final_b200/cpp/b2_layers.h): reference
+class names and entry points over the C ABI.
+
+CPU: the adapter library and its driver are built and load without a GPU.
+GPU: b2_layers_run constructs SparseMoeBlock(layer_idx) / MLP(w1, w2, w3) from
+weights stored under the reference's tensor names (src/layer.cu:1274-1297),
+runs init_gpu() + forward_gpu(x, y, 1, T, H, stream) as
+DecoderLayer::forward_gpu does, and y is compared with the CPU oracle
+(tolerance 1e-2 bf16 / 5e-3 TF32, as for the C ABI tests).
+"""
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+LIBDIR = ROOT / "final_b200" / "lib"
+RUN = LIBDIR / "b2_layers_run"
+TOL = {"bf16": 1e-2, "tf32": 5e-3}
+
+
+def _built():
+    from final_b200 import build as b
+    b.build()
+    b.build_cpp()
+
+
+def test_adapter_builds_and_loads():
+    _built()
+    ctypes.CDLL(str(LIBDIR / "libb2layers.so"))
+    r = subprocess.run([str(RUN), "--help"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "usage" in r.stderr
+
+
+def _store(d: Path, name: str, a: np.ndarray) -> None:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    (d / f"{name}.f32").write_bytes(a.tobytes())
+    (d / f"{name}.shape").write_text(" ".join(str(s) for s in a.shape))
+
+
+def _run(kind, d, layer, x, dtype):
+    xf, yf = d / "x.f32", d / "y.f32"
+    xf.write_bytes(np.ascontiguousarray(x, dtype=np.float32).tobytes())
+    r = subprocess.run([str(RUN), kind, str(d), str(layer), str(x.shape[0]), str(xf), str(yf),
+                        dtype], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return np.frombuffer(yf.read_bytes(), dtype=np.float32).reshape(x.shape)
+
+
+def _rel(a, b):
+    return float(np.abs(a.astype(np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["bf16", "tf32"])
+def test_cpp_sparse_moe_block(cuda_dev, oracle, tmp_path, dtype):
+    _built()
+    T, H, E, I, layer = 77, 512, 8, 256, 3
+    inp = oracle.moe_inputs(T, H, E, I, seed=21)
+    pre = f"layers.{layer}.feed_forward."
+    _store(tmp_path, pre + "gate.weight", inp["gate"])
+    _store(tmp_path, pre + "expert_bias", inp["bias"])
+    for e in range(E):
+        for w in ("w1", "w2", "w3"):
+            _store(tmp_path, f"{pre}experts.{e}.{w}.weight", inp[w][e])
+    y = _run("moe", tmp_path, layer, inp["x"], dtype)
+    ref = oracle.moe_forward(inp["x"], inp["gate"], inp["bias"], inp["w1"], inp["w2"], inp["w3"])
+    assert _rel(y, ref["y"]) < TOL[dtype]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["bf16", "tf32"])
+def test_cpp_mlp(cuda_dev, oracle, tmp_path, dtype):
+    _built()
+    T, H, I, layer = 130, 1024, 1536, 0
+    x = oracle.randn((T, H), 8, oracle.S_X)
+    w1 = oracle.randn((I, H), 8, oracle.S_W1, 0.02)
+    w3 = oracle.randn((I, H), 8, oracle.S_W3, 0.02)
+    w2 = oracle.randn((H, I), 8, oracle.S_W2, 0.02)
+    pre = f"layers.{layer}.feed_forward."
+    for n, a in (("w1", w1), ("w2", w2), ("w3", w3)):
+        _store(tmp_path, f"{pre}{n}.weight", a)
+    y = _run("mlp", tmp_path, layer, x, dtype)
+    assert _rel(y, oracle.dense_mlp(x, w1, w3, w2)) < TOL[dtype]
