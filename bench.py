@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--no-dense", action="store_true", help="skip the dense GEMM sweep")
     p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
                    help="expert placement when --gpus > 1")
+    p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
+                   help="only time b2_gemm_nt on one dense shape (bf16 operands), "
+                        "e.g. for a profiler capture of the dense kernel")
     return p.parse_args()
 
 
@@ -484,6 +487,30 @@ def dense_sweep(dev, K=2048, reps=10):
     return res
 
 
+def gemm_only(args, dev):
+    """One dense shape, bf16 operands, fp32 C: warm-up + timed launches."""
+    import torch
+    from final_b200 import gemm_nt, to_bf16
+    M, N, Kd = args.gemm
+    g = torch.Generator(device=dev).manual_seed(2)
+    A = to_bf16(torch.randn(M, Kd, device=dev, generator=g))
+    B = to_bf16(torch.randn(N, Kd, device=dev, generator=g) * 0.02)
+    C = torch.empty(M, N, device=dev)
+    for _ in range(args.warmup):
+        gemm_nt(A, B, out=C)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        gemm_nt(A, B, out=C)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    return {"metric": "dense_gemm_tflops", "M": M, "N": N, "K": Kd, "ms": ms,
+            "tflops": 2.0 * M * N * Kd / (ms / 1e3) / 1e12, "steps": args.steps,
+            "warmup": args.warmup}
+
+
 def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
     """Dense SwiGLU MLP of the layers without experts (I = 7168) over T tokens
     on the same GEMM core: tokens/s and TFLOP/s (6*T*H*I FLOP per forward)."""
@@ -658,6 +685,9 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
+    if args.gemm:
+        print(json.dumps(gemm_only(args, dev)), flush=True)
+        return 0
     try:
         out = run_ours(args, rank, world, dev)
         if rank == 0:
