@@ -21,7 +21,7 @@ EXPORTED = (
     "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
-    "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy",
+    "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy", "b2_flag_wait",
     # include/b2mlp.h
     "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_device_bytes",
     "b2_mlp_destroy",
@@ -106,6 +106,7 @@ def load(path: Path | None = None):
                                  C.POINTER(vp)]
     lib.b2_ep_forward.argtypes = [vp, vp, vp, i, vp]
     lib.b2_ep_set_timeout.argtypes = [vp, C.c_double]
+    lib.b2_flag_wait.argtypes = [vp, vp, i, C.c_uint64, C.c_double, vp, vp]
     lib.b2_ep_last_plan.argtypes = [vp, C.POINTER(EpPlan)]
     lib.b2_ep_layer.argtypes = [vp]
     lib.b2_ep_layer.restype = vp
@@ -125,7 +126,7 @@ def load(path: Path | None = None):
                  "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
                  "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc",
                  "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
-                 "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy",
+                 "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy", "b2_flag_wait",
                  "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_destroy"):
         getattr(lib, name).restype = i
     _lib = lib

@@ -252,6 +252,18 @@ static __global__ void wait_flags_kernel(const volatile uint64_t *flags, const i
   __threadfence_system();
 }
 
+extern "C" b2_status b2_flag_wait(const uint64_t *flags, const int *idx, int n, uint64_t target,
+                                  double timeout_s, int *status, b2_stream stream) {
+  if (n < 0 || n > 1024 || (n > 0 && (!flags || !idx || !status)) || !(timeout_s > 0) ||
+      timeout_s > 600)
+    return B2_ERR_INVALID;
+  if (n == 0) return B2_OK;
+  wait_flags_kernel<<<1, 32 * ((n + 31) / 32), 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      flags, idx, n, target, (uint64_t)(timeout_s * 1e9), status);
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
 extern "C" b2_status b2_ep_unique_id(void *id_out) {
   if (!id_out) return B2_ERR_INVALID;
   if (!nccl().ok) return B2_ERR_COMM;

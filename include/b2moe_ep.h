@@ -85,6 +85,18 @@ b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
 b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int num_tokens,
                         b2_stream stream);
 
+/* The bounded device-side wait of the exchange on its own: one thread per
+ * flag waits until flags[idx[i]] >= target (device pointers; n <= 1024) and
+ * gives up after timeout_s (<= 600) seconds, recording 0x105 in the device
+ * int *status (first error wins).  The kernel always returns, so a flag that
+ * no peer ever writes leaves the context usable; the caller reads *status
+ * after synchronising `stream`.  No counterpart in the reference, whose
+ * pipeline stages wait on CUDA events without a bound
+ * (src/model.cu:441-445). */
+b2_status b2_flag_wait(const uint64_t *flags, const int *idx, int n,
+                       uint64_t target, double timeout_s, int *status,
+                       b2_stream stream);
+
 /* Host-side bound (seconds) on every wait for the peers (default 60). */
 b2_status b2_ep_set_timeout(b2_ep *ep, double seconds);
 

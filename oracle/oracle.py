@@ -51,6 +51,11 @@ def lib():
     o.b2o_randn.argtypes = [f32p, C.c_size_t, C.c_uint64, C.c_uint64, C.c_float]
     o.b2o_randu.argtypes = [f64p, C.c_size_t, C.c_uint64, C.c_uint64]
     o.b2o_set_num_threads.argtypes = [C.c_int]
+    o.b2o_rmsnorm.argtypes = [f32p, f32p, f32p, C.c_int, C.c_int]
+    o.b2o_rope_tables.argtypes = [f32p, f32p, C.c_int, C.c_int, C.c_float]
+    o.b2o_attention_core.argtypes = [f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     f32p, f32p, f32p, f32p, f32p]
+    o.b2o_shortconv_core.argtypes = [f32p, f32p, C.c_int, C.c_int, C.c_int, C.c_int, f32p]
     _o = o
     return o
 
@@ -213,6 +218,60 @@ def moe_forward(x, gate, bias, w1, w2, w3, K=4, routed_scale=1.0, tile=128):
                 mtile_offsets=toff, sorted_token=st, sorted_w=sw, token_slot=slot)
 
 
+# ------------------------------------------------------ LFM2 decoder glue
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def rmsnorm(x, w):
+    """rms_norm_kernel (src/layer.cu:144-191) over the last axis."""
+    x = _f32(x)
+    dim = x.shape[-1]
+    y = np.empty_like(x)
+    lib().b2o_rmsnorm(x, _f32(w), y, x.size // dim, dim)
+    return y
+
+
+def rope_tables(npos, head_dim=64, theta=1000000.0):
+    """RotaryEmbedding::init_gpu tables (src/layer.cu:1167-1190), [npos][head_dim]."""
+    c = np.empty((npos, head_dim), dtype=np.float32)
+    s = np.empty((npos, head_dim), dtype=np.float32)
+    lib().b2o_rope_tables(c, s, npos, head_dim, theta)
+    return c, s
+
+
+def attention_core(qkv, B, S, Hq, Hkv, q_ln, k_ln, cos, sin, hd=64):
+    out = np.zeros((B * S, Hq * hd), dtype=np.float32)
+    lib().b2o_attention_core(_f32(qkv), B, S, Hq, Hkv, hd, _f32(q_ln), _f32(k_ln), _f32(cos),
+                             _f32(sin), out)
+    return out
+
+
+def attention_block(x, wq, wk, wv, wo, q_ln, k_ln, cos, sin, B, S, want_core=False):
+    """Attention::forward_gpu (src/layer.cu:1584-1659): projections by the
+    sequential-k GEMM, q/k norm + RoPE + causal GQA core, out projection."""
+    hd = q_ln.shape[0]
+    Hq, Hkv = wq.shape[0] // hd, wk.shape[0] // hd
+    qkv = np.concatenate([gemm_nt(x, wq), gemm_nt(x, wk), gemm_nt(x, wv)], axis=1)
+    core = attention_core(qkv, B, S, Hq, Hkv, q_ln, k_ln, cos, sin, hd)
+    y = gemm_nt(core, wo)
+    return (y, core) if want_core else y
+
+
+def shortconv_core(in_proj_out, conv_w, B, S):
+    H, L = conv_w.shape[0], conv_w.shape[-1]
+    y = np.empty((B * S, H), dtype=np.float32)
+    lib().b2o_shortconv_core(_f32(in_proj_out), _f32(conv_w.reshape(H, L)), B, S, H, L, y)
+    return y
+
+
+def shortconv_block(x, in_w, conv_w, out_w, B, S, want_core=False):
+    """ShortConv::forward_gpu (src/layer.cu:1735-1777)."""
+    core = shortconv_core(gemm_nt(x, in_w), conv_w, B, S)
+    y = gemm_nt(core, out_w)
+    return (y, core) if want_core else y
+
+
 # ------------------------------------------------------ reference kernels
 def ref_lib():
     """The reference's own CUDA kernels compiled from its sources (oracle/_ref).
@@ -229,6 +288,13 @@ def ref_lib():
     r.ref_moe_create.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, i, i, C.POINTER(vp)]
     r.ref_moe_destroy.argtypes = [vp]
     r.ref_moe_forward.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, vp]
+    r.ref_rmsnorm.argtypes = [vp, vp, vp, i, i, vp]
+    r.ref_add.argtypes = [vp, vp, vp, i, vp]
+    r.ref_embed.argtypes = [vp, vp, vp, i, i, vp]
+    r.ref_rope_tables.argtypes = [vp, vp, i]
+    r.ref_attention.argtypes = [vp] * 11 + [i] * 5 + [vp]
+    r.ref_shortconv.argtypes = [vp] * 6 + [i] * 3 + [vp]
+    r.ref_mlp.argtypes = [vp] * 5 + [i] * 3 + [vp]
     _r = r
     return r
 

@@ -14,6 +14,10 @@
 #include <cuda_runtime.h>
 #include <cstdio>
 #include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "layer.h"  // RotaryEmbedding (reference header)
 
 // Kernels defined in the reference's src/layer.cu (signatures as declared there).
 __global__ void attn_matmul_tiled_kernel(float *out, const float *A,
@@ -52,11 +56,38 @@ __global__ void moe_gather_deterministic_kernel(
     const int *__restrict__ token_expert_pos,
     const float *__restrict__ topk_weights, int num_tokens, int hidden_size,
     int k_experts);
+__global__ void rms_norm_kernel(float *out, const float *in, const float *weight,
+                                int total_rows, int hidden_dim);
+__global__ void rope_transpose_kernel(float *out, const float *in, const float *cos,
+                                      const float *sin, int batch, int seq_len,
+                                      int num_heads, int head_dim);
+__global__ void transpose_v_kernel(float *out, const float *in, int batch,
+                                   int seq_len, int num_heads, int head_dim);
+__global__ void fused_attn_gqa_kernel(float *__restrict__ output,
+                                      const float *__restrict__ Q,
+                                      const float *__restrict__ K,
+                                      const float *__restrict__ V, int seq_len,
+                                      int head_dim, int num_heads,
+                                      int num_kv_heads, float scale);
+__global__ void conv_transpose_split_kernel(float *Bx, float *C, const float *in_proj,
+                                            int batch, int seq_len, int hidden_size);
+__global__ void causal_conv1d_kernel(float *out, const float *input, const float *weight,
+                                     int batch, int hidden_size, int seq_len,
+                                     int kernel_size);
+__global__ void conv_gating_transpose_kernel(float *out, const float *C,
+                                             const float *conv_out, int batch,
+                                             int hidden_size, int seq_len);
+__global__ void add_kernel(float *out, const float *a, const float *b, int n);
+__global__ void moe_swiglu_kernel(float *interm, const float *w1_out,
+                                  const float *w3_out, int size);
 // Defined in the reference's src/model.cu.
 __global__ void lm_head_gemm_kernel(float *__restrict__ C,
                                     const float *__restrict__ A,
                                     const float *__restrict__ B, int M, int N,
                                     int K);
+__global__ void embedding_lookup_kernel(float *hidden_states, const int *input_ids,
+                                        const float *embed_table, int seq_len,
+                                        int hidden_size);
 
 #define RH_CHECK(call)                                                        \
   do {                                                                        \
@@ -207,6 +238,157 @@ int ref_moe_forward(void *h, const float *x, float *y, int num_tokens,
   if (offsets_out) RH_CHECK(cudaMemcpyAsync(offsets_out, m->offsets, E * sizeof(int), cudaMemcpyDeviceToDevice, stream));
   if (tok_pos_out) RH_CHECK(cudaMemcpyAsync(tok_pos_out, m->tok_pos, tk * sizeof(int), cudaMemcpyDeviceToDevice, stream));
   if (sorted_idx_out) RH_CHECK(cudaMemcpyAsync(sorted_idx_out, m->sorted_idx, tk * sizeof(int), cudaMemcpyDeviceToDevice, stream));
+  return 0;
+}
+
+// ------------------------------------------------------------------ glue
+// RMSNorm::forward_gpu (src/layer.cu:1144-1148).
+int ref_rmsnorm(float *y, const float *x, const float *w, int rows, int dim,
+                cudaStream_t stream) {
+  rms_norm_kernel<<<rows, 256, 0, stream>>>(y, x, w, rows, dim);
+  RH_CHECK(cudaGetLastError());
+  return 0;
+}
+
+// add_kernel as DecoderLayer::forward_gpu launches it (src/layer.cu:1905-1918).
+int ref_add(float *out, const float *a, const float *b, int n, cudaStream_t stream) {
+  add_kernel<<<(n + 255) / 256, 256, 0, stream>>>(out, a, b, n);
+  RH_CHECK(cudaGetLastError());
+  return 0;
+}
+
+// embedding_lookup_kernel as worker_stage launches it (src/model.cu:409-412).
+int ref_embed(float *hidden, const int *ids, const float *table, int tokens,
+              int hidden_size, cudaStream_t stream) {
+  int n = tokens * hidden_size;
+  embedding_lookup_kernel<<<(n + 255) / 256, 256, 0, stream>>>(hidden, ids, table,
+                                                               tokens, hidden_size);
+  RH_CHECK(cudaGetLastError());
+  return 0;
+}
+
+// The reference's own RotaryEmbedding (constructed and initialised exactly as
+// a pipeline stage does, src/model.cu:298-300); copies its first npos rows of
+// the cos / sin tables ([npos][HEAD_DIM] fp32) to host buffers.
+int ref_rope_tables(float *cos_out, float *sin_out, int npos) {
+  RotaryEmbedding r;
+  r.init_gpu();
+  RH_CHECK(cudaMemcpy(cos_out, r.cos_gpu_, (size_t)npos * HEAD_DIM * sizeof(float),
+                      cudaMemcpyDeviceToHost));
+  RH_CHECK(cudaMemcpy(sin_out, r.sin_gpu_, (size_t)npos * HEAD_DIM * sizeof(float),
+                      cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+// Attention::forward_gpu (src/layer.cu:1584-1659), launch for launch, on
+// caller buffers: x [T,H]; wq [Hq*64,H], wk/wv [Hkv*64,H], wo [H,Hq*64];
+// q_ln/k_ln [64]; cos/sin [>=S][64]; y [T,H].  The reference kernel serves
+// exactly seq_len 16 (block (32,16), 16 logits per thread): other lengths are
+// refused.  `core_out` (may be null) receives the attention output before the
+// out projection, [T, Hq*64].
+int ref_attention(const float *x, const float *wq, const float *wk, const float *wv,
+                  const float *wo, const float *q_ln, const float *k_ln,
+                  const float *cos, const float *sin, float *y, float *core_out,
+                  int batch, int seq_len, int hidden, int num_heads, int num_kv_heads,
+                  cudaStream_t stream) {
+  if (seq_len != 16) return -3;
+  const int hd = 64, T = batch * seq_len;
+  const size_t qn = (size_t)T * num_heads * hd, kn = (size_t)T * num_kv_heads * hd;
+  float *q, *k, *v, *qn_, *kn_, *qt, *kt, *vt, *ot;
+  RH_CHECK(cudaMalloc(&q, qn * 4));
+  RH_CHECK(cudaMalloc(&k, kn * 4));
+  RH_CHECK(cudaMalloc(&v, kn * 4));
+  RH_CHECK(cudaMalloc(&qn_, qn * 4));
+  RH_CHECK(cudaMalloc(&kn_, kn * 4));
+  RH_CHECK(cudaMalloc(&qt, qn * 4));
+  RH_CHECK(cudaMalloc(&kt, kn * 4));
+  RH_CHECK(cudaMalloc(&vt, kn * 4));
+  RH_CHECK(cudaMalloc(&ot, qn * 4));
+  dim3 block(16, 16);
+  dim3 grid_q((num_heads * hd + 127) / 128, (T + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_q, block, 0, stream>>>(q, x, wq, T, num_heads * hd, hidden);
+  dim3 grid_k((num_kv_heads * hd + 127) / 128, (T + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_k, block, 0, stream>>>(k, x, wk, T, num_kv_heads * hd, hidden);
+  attn_matmul_tiled_kernel<<<grid_k, block, 0, stream>>>(v, x, wv, T, num_kv_heads * hd, hidden);
+  rms_norm_kernel<<<T * num_heads, 256, 0, stream>>>(qn_, q, q_ln, T * num_heads, hd);
+  rms_norm_kernel<<<T * num_kv_heads, 256, 0, stream>>>(kn_, k, k_ln, T * num_kv_heads, hd);
+  int rq = batch * num_heads * seq_len * (hd / 2);
+  rope_transpose_kernel<<<(rq + 255) / 256, 256, 0, stream>>>(qt, qn_, cos, sin, batch,
+                                                              seq_len, num_heads, hd);
+  int rk = batch * num_kv_heads * seq_len * (hd / 2);
+  rope_transpose_kernel<<<(rk + 255) / 256, 256, 0, stream>>>(kt, kn_, cos, sin, batch,
+                                                              seq_len, num_kv_heads, hd);
+  int vtot = batch * num_kv_heads * seq_len * hd;
+  transpose_v_kernel<<<(vtot + 255) / 256, 256, 0, stream>>>(vt, v, batch, seq_len,
+                                                             num_kv_heads, hd);
+  dim3 grid_attn(batch, num_heads);
+  dim3 block_attn(32, 16);
+  size_t smem = 2 * seq_len * hd * sizeof(float);
+  fused_attn_gqa_kernel<<<grid_attn, block_attn, smem, stream>>>(
+      ot, qt, kt, vt, seq_len, hd, num_heads, num_kv_heads, 1.0f / sqrtf((float)hd));
+  dim3 grid_o((hidden + 127) / 128, (T + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_o, block, 0, stream>>>(y, ot, wo, T, hidden, num_heads * hd);
+  RH_CHECK(cudaGetLastError());
+  if (core_out)
+    RH_CHECK(cudaMemcpyAsync(core_out, ot, qn * 4, cudaMemcpyDeviceToDevice, stream));
+  RH_CHECK(cudaStreamSynchronize(stream));
+  float *bufs[] = {q, k, v, qn_, kn_, qt, kt, vt, ot};
+  for (float *b : bufs) cudaFree(b);
+  return 0;
+}
+
+// ShortConv::forward_gpu (src/layer.cu:1735-1777), launch for launch:
+// x [T,H]; in_w [3H,H]; conv_w [H][3]; out_w [H,H]; y [T,H].  `core_out`
+// (may be null) receives the gated conv output before the out projection.
+int ref_shortconv(const float *x, const float *in_w, const float *conv_w,
+                  const float *out_w, float *y, float *core_out, int batch,
+                  int seq_len, int hidden, cudaStream_t stream) {
+  const int T = batch * seq_len;
+  float *ip, *bx, *c, *co, *yt;
+  RH_CHECK(cudaMalloc(&ip, (size_t)T * 3 * hidden * 4));
+  RH_CHECK(cudaMalloc(&bx, (size_t)T * hidden * 4));
+  RH_CHECK(cudaMalloc(&c, (size_t)T * hidden * 4));
+  RH_CHECK(cudaMalloc(&co, (size_t)T * hidden * 4));
+  RH_CHECK(cudaMalloc(&yt, (size_t)T * hidden * 4));
+  dim3 block(16, 16);
+  dim3 grid_in((3 * hidden + 127) / 128, (T + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_in, block, 0, stream>>>(ip, x, in_w, T, 3 * hidden, hidden);
+  int tot = T * hidden;
+  conv_transpose_split_kernel<<<(tot + 255) / 256, 256, 0, stream>>>(bx, c, ip, batch,
+                                                                     seq_len, hidden);
+  causal_conv1d_kernel<<<(tot + 255) / 256, 256, 0, stream>>>(co, bx, conv_w, batch, hidden,
+                                                              seq_len, CONV_KERNEL);
+  conv_gating_transpose_kernel<<<(tot + 255) / 256, 256, 0, stream>>>(yt, c, co, batch,
+                                                                      hidden, seq_len);
+  dim3 grid_out((hidden + 127) / 128, (T + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_out, block, 0, stream>>>(y, yt, out_w, T, hidden, hidden);
+  RH_CHECK(cudaGetLastError());
+  if (core_out)
+    RH_CHECK(cudaMemcpyAsync(core_out, yt, (size_t)tot * 4, cudaMemcpyDeviceToDevice, stream));
+  RH_CHECK(cudaStreamSynchronize(stream));
+  float *bufs[] = {ip, bx, c, co, yt};
+  for (float *b : bufs) cudaFree(b);
+  return 0;
+}
+
+// MLP::forward_gpu (src/layer.cu:1233-1269) with the scratch
+// DecoderLayer::init_gpu gives it (:1860-1866): gate/up [T, inter] each.
+int ref_mlp(const float *x, const float *w1, const float *w2, const float *w3, float *y,
+            int tokens, int hidden, int inter, cudaStream_t stream) {
+  float *tmp;
+  RH_CHECK(cudaMalloc(&tmp, (size_t)tokens * inter * 2 * sizeof(float)));
+  float *gate = tmp, *up = tmp + (size_t)tokens * inter;
+  dim3 block(16, 16);
+  dim3 grid_gate((inter + 127) / 128, (tokens + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_gate, block, 0, stream>>>(gate, x, w1, tokens, inter, hidden);
+  attn_matmul_tiled_kernel<<<grid_gate, block, 0, stream>>>(up, x, w3, tokens, inter, hidden);
+  int tot = tokens * inter;
+  moe_swiglu_kernel<<<(tot + 255) / 256, 256, 0, stream>>>(gate, gate, up, tot);
+  dim3 grid_down((hidden + 127) / 128, (tokens + 127) / 128);
+  attn_matmul_tiled_kernel<<<grid_down, block, 0, stream>>>(y, gate, w2, tokens, hidden, inter);
+  RH_CHECK(cudaGetLastError());
+  RH_CHECK(cudaStreamSynchronize(stream));
+  cudaFree(tmp);
   return 0;
 }
 
