@@ -25,6 +25,12 @@ EXPORTED = (
     # include/b2mlp.h
     "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_device_bytes",
     "b2_mlp_destroy",
+    # include/b2lfm2.h
+    "b2_rmsnorm", "b2_add_rmsnorm", "b2_rope_tables", "b2_embed",
+    "b2_attn_create", "b2_attn_forward", "b2_attn_destroy",
+    "b2_conv_create", "b2_conv_forward", "b2_conv_destroy",
+    "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex", "b2_lfm2_get_status",
+    "b2_lfm2_device_bytes", "b2_lfm2_destroy",
 )
 
 EP_MAX_WORLD = 64
@@ -48,6 +54,28 @@ class MoeDesc(C.Structure):
 class MlpDesc(C.Structure):
     _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("max_tokens", C.c_int),
                 ("dtype", C.c_int)]
+
+
+class AttnDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("num_heads", C.c_int), ("num_kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("max_tokens", C.c_int), ("eps", C.c_float)]
+
+
+class ConvDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("kernel", C.c_int), ("max_tokens", C.c_int)]
+
+
+class Lfm2Desc(C.Structure):
+    _fields_ = [("vocab", C.c_int), ("hidden", C.c_int), ("num_layers", C.c_int),
+                ("num_heads", C.c_int), ("num_kv_heads", C.c_int), ("dense_inter", C.c_int),
+                ("moe_inter", C.c_int), ("num_experts", C.c_int), ("top_k", C.c_int),
+                ("num_dense_layers", C.c_int), ("max_batch", C.c_int), ("max_seq", C.c_int),
+                ("eps", C.c_float), ("rope_theta", C.c_float), ("routed_scale", C.c_float),
+                ("use_expert_bias", C.c_int), ("layer_types", C.c_int * 64), ("dtype", C.c_int)]
+
+
+# const float *(*)(void *ctx, const char *name, int64_t numel)
+WEIGHT_FN = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_char_p, C.c_int64)
 
 
 class MoeTrace(C.Structure):
@@ -117,6 +145,30 @@ def load(path: Path | None = None):
     lib.b2_mlp_device_bytes.argtypes = [vp]
     lib.b2_mlp_device_bytes.restype = sz
     lib.b2_mlp_destroy.argtypes = [vp]
+    f = C.c_float
+    lib.b2_rmsnorm.argtypes = [vp, vp, vp, i, i, f, vp]
+    lib.b2_add_rmsnorm.argtypes = [vp, vp, vp, vp, vp, i, i, f, vp]
+    lib.b2_rope_tables.argtypes = [vp, vp, i, i, f]
+    lib.b2_embed.argtypes = [vp, vp, vp, i, i, i, vp, vp]
+    lib.b2_attn_create.argtypes = [C.POINTER(AttnDesc), vp, vp, vp, vp, vp, vp, i, vp,
+                                   C.POINTER(vp)]
+    lib.b2_attn_forward.argtypes = [vp, vp, vp, vp, vp, i, i, vp]
+    lib.b2_attn_destroy.argtypes = [vp]
+    lib.b2_conv_create.argtypes = [C.POINTER(ConvDesc), vp, vp, vp, i, vp, C.POINTER(vp)]
+    lib.b2_conv_forward.argtypes = [vp, vp, vp, i, i, vp]
+    lib.b2_conv_destroy.argtypes = [vp]
+    lib.b2_lfm2_create.argtypes = [C.POINTER(Lfm2Desc), WEIGHT_FN, vp, i, vp, C.POINTER(vp)]
+    lib.b2_lfm2_forward.argtypes = [vp, vp, i, i, vp, vp]
+    lib.b2_lfm2_forward_ex.argtypes = [vp, vp, i, i, vp, vp, vp]
+    lib.b2_lfm2_get_status.argtypes = [vp, vp, C.POINTER(i)]
+    lib.b2_lfm2_device_bytes.argtypes = [vp]
+    lib.b2_lfm2_device_bytes.restype = sz
+    lib.b2_lfm2_destroy.argtypes = [vp]
+    for name in ("b2_rmsnorm", "b2_add_rmsnorm", "b2_rope_tables", "b2_embed", "b2_attn_create",
+                 "b2_attn_forward", "b2_attn_destroy", "b2_conv_create", "b2_conv_forward",
+                 "b2_conv_destroy", "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex",
+                 "b2_lfm2_get_status", "b2_lfm2_destroy"):
+        getattr(lib, name).restype = i
     lib.b2_kernel_launch_count.restype = C.c_uint64
     lib.b2_moe_tile_rows.restype = i
     lib.b2_status_string.argtypes = [i]

@@ -23,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
 
-SOURCES = ["b2moe_api.cu", "ep.cu", "noalloc.cu", "mlp.cu"]
+SOURCES = ["b2moe_api.cu", "ep.cu", "noalloc.cu", "mlp.cu", "lfm2.cu"]
 
 
 def _needs_rebuild(target: Path, deps) -> bool:

@@ -1,0 +1,234 @@
+"""Python host mirror of the reference's decoder operators around the MoE:
+``RMSNorm``, ``rope_tables`` (RotaryEmbedding), ``Attention``, ``ShortConv``
+and the whole-model ``LFM2Model`` (include/layer.h:10-176,
+include/model.h:28-36 of the reference).
+
+The weights are handed over once; ``forward_gpu`` runs on caller-owned fp32
+device buffers, stream-ordered, with the reference's argument order.  All
+compute goes through the C ABI of include/b2lfm2.h; errors raise B2Error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Callable, Dict, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import AttnDesc, ConvDesc, Lfm2Desc, WEIGHT_FN, check
+from .moe import _DT, _stream_ptr
+
+# The reference model (include/config.h:3-31).
+LAYER_TYPES = (1, 1, 0, 1, 1, 1, 0, 1, 1, 1, 0, 1, 1, 1, 0, 1, 1, 1, 0, 1, 1, 0, 1, 1)
+CONFIG = dict(vocab=65536, hidden=2048, num_layers=24, num_heads=32, num_kv_heads=8,
+              dense_inter=7168, moe_inter=1792, num_experts=32, top_k=4, num_dense_layers=2,
+              eps=1e-5, rope_theta=1e6, routed_scale=1.0, use_expert_bias=1)
+
+
+def _vp(t) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p()
+
+
+def _dev_f32(t: torch.Tensor) -> None:
+    assert t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5,
+            stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """RMSNorm over the last axis (RMSNorm::forward_gpu, src/layer.cu:1144-1148)."""
+    _dev_f32(x)
+    _dev_f32(w)
+    dim = x.shape[-1]
+    y = torch.empty_like(x)
+    check(_lib.load().b2_rmsnorm(_vp(x), _vp(w), _vp(y), x.numel() // dim, dim, eps,
+                                 C.c_void_p(_stream_ptr(stream))), "b2_rmsnorm")
+    return y
+
+
+def rope_tables(max_pos: int, head_dim: int = 64, base: float = 1e6):
+    """Host cos / sin tables [max_pos][head_dim] (RotaryEmbedding::init_gpu)."""
+    c = np.empty((max_pos, head_dim), dtype=np.float32)
+    s = np.empty_like(c)
+    check(_lib.load().b2_rope_tables(c.ctypes.data, s.ctypes.data, max_pos, head_dim, base),
+          "b2_rope_tables")
+    return c, s
+
+
+def embed(ids: torch.Tensor, table: torch.Tensor,
+          stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """hidden[t] = table[ids[t]] (embedding_lookup_kernel, src/model.cu:18-31)."""
+    _dev_f32(table)
+    ids = ids.to(torch.int32).contiguous()
+    V, H = table.shape
+    out = torch.empty(ids.numel(), H, dtype=torch.float32, device=table.device)
+    status = torch.zeros(1, dtype=torch.int32, device=table.device)
+    check(_lib.load().b2_embed(_vp(ids), _vp(table), _vp(out), ids.numel(), H, V, _vp(status),
+                               C.c_void_p(_stream_ptr(stream))), "b2_embed")
+    return out
+
+
+class _Handle:
+    _destroy = ""
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            getattr(self.lib, self._destroy)(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Attention(_Handle):
+    """GQA attention block (Attention, include/layer.h:126-159): wq [Hq*64, H],
+    wk / wv [Hkv*64, H], wo [H, Hq*64], q_ln / k_ln [64], fp32 on one device."""
+    _destroy = "b2_attn_destroy"
+
+    def __init__(self, wq, wk, wv, wo, q_ln, k_ln, *, max_tokens: int, eps: float = 1e-5,
+                 stream: Optional[torch.cuda.Stream] = None):
+        self.lib = _lib.load()
+        for t in (wq, wk, wv, wo, q_ln, k_ln):
+            _dev_f32(t)
+        self.H = wq.shape[1]
+        d = AttnDesc(hidden=self.H, num_heads=wq.shape[0] // 64, num_kv_heads=wk.shape[0] // 64,
+                     head_dim=64, max_tokens=max_tokens, eps=eps)
+        h = C.c_void_p()
+        with torch.cuda.device(wq.device):
+            check(self.lib.b2_attn_create(C.byref(d), _vp(wq), _vp(wk), _vp(wv), _vp(wo),
+                                          _vp(q_ln), _vp(k_ln), 0,
+                                          C.c_void_p(_stream_ptr(stream)), C.byref(h)),
+                  "b2_attn_create")
+        self._h = h
+
+    def forward_gpu(self, x, cos, sin, output, batch: int, seq_len: int, hidden_size: int,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        assert hidden_size == self.H
+        check(self.lib.b2_attn_forward(self._h, _vp(x), _vp(cos), _vp(sin), _vp(output), batch,
+                                       seq_len, C.c_void_p(_stream_ptr(stream))),
+              "b2_attn_forward")
+
+    def forward(self, x, cos, sin, batch: int, seq_len: int) -> torch.Tensor:
+        y = torch.empty(batch * seq_len, self.H, dtype=torch.float32, device=x.device)
+        self.forward_gpu(x, cos, sin, y, batch, seq_len, self.H)
+        return y
+
+
+class ShortConv(_Handle):
+    """Gated short-convolution block (ShortConv, include/layer.h:161-194):
+    conv_w [H, 1, 3], in_w [3H, H], out_w [H, H], fp32 on one device."""
+    _destroy = "b2_conv_destroy"
+
+    def __init__(self, conv_w, in_w, out_w, *, max_tokens: int,
+                 stream: Optional[torch.cuda.Stream] = None):
+        self.lib = _lib.load()
+        for t in (conv_w, in_w, out_w):
+            _dev_f32(t)
+        self.H = out_w.shape[0]
+        d = ConvDesc(hidden=self.H, kernel=conv_w.shape[-1], max_tokens=max_tokens)
+        h = C.c_void_p()
+        with torch.cuda.device(in_w.device):
+            check(self.lib.b2_conv_create(C.byref(d), _vp(conv_w), _vp(in_w), _vp(out_w), 0,
+                                          C.c_void_p(_stream_ptr(stream)), C.byref(h)),
+                  "b2_conv_create")
+        self._h = h
+
+    def forward_gpu(self, x, y, batch: int, seq_len: int, hidden_size: int,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        assert hidden_size == self.H
+        check(self.lib.b2_conv_forward(self._h, _vp(x), _vp(y), batch, seq_len,
+                                       C.c_void_p(_stream_ptr(stream))), "b2_conv_forward")
+
+    def forward(self, x, batch: int, seq_len: int) -> torch.Tensor:
+        y = torch.empty(batch * seq_len, self.H, dtype=torch.float32, device=x.device)
+        self.forward_gpu(x, y, batch, seq_len, self.H)
+        return y
+
+
+class LFM2Model(_Handle):
+    """The whole model on one GPU (LFM2Model, include/model.h:28-36).
+
+    ``weights(name, numel)`` returns the tensor of that reference name (an
+    fp32 torch tensor on the device, or a numpy array with
+    ``weights_on_host=True``) or None when the model has no such tensor; the
+    returned objects are kept alive until construction ends.  Other
+    keywords override the reference configuration (``CONFIG``)."""
+    _destroy = "b2_lfm2_destroy"
+
+    def __init__(self, weights: Callable[[str, int], object], *, max_batch: int, max_seq: int,
+                 weights_on_host: bool = False, layer_types=LAYER_TYPES, dtype: str = "bf16",
+                 device: Optional[torch.device] = None,
+                 stream: Optional[torch.cuda.Stream] = None, **cfg):
+        self.lib = _lib.load()
+        c = dict(CONFIG)
+        c.update(cfg)
+        self.cfg = c
+        self.layers = c["num_layers"]
+        d = Lfm2Desc(vocab=c["vocab"], hidden=c["hidden"], num_layers=c["num_layers"],
+                     num_heads=c["num_heads"], num_kv_heads=c["num_kv_heads"],
+                     dense_inter=c["dense_inter"], moe_inter=c["moe_inter"],
+                     num_experts=c["num_experts"], top_k=c["top_k"],
+                     num_dense_layers=c["num_dense_layers"], max_batch=max_batch,
+                     max_seq=max_seq, eps=c["eps"], rope_theta=c["rope_theta"],
+                     routed_scale=c["routed_scale"], use_expert_bias=c["use_expert_bias"],
+                     dtype=_DT[dtype])
+        for i in range(c["num_layers"]):
+            d.layer_types[i] = int(layer_types[i])
+        self.vocab, self.H = c["vocab"], c["hidden"]
+        self.max_batch, self.max_seq = max_batch, max_seq
+        keep: Dict[str, object] = {}
+
+        def get(_ctx, name, numel):
+            t = weights(name.decode(), int(numel))
+            if t is None:
+                return None
+            if isinstance(t, np.ndarray):
+                assert weights_on_host and t.dtype == np.float32 and t.flags.c_contiguous
+                assert t.size == numel, (name, t.size, numel)
+                keep[name] = t
+                return t.ctypes.data
+            assert not weights_on_host
+            _dev_f32(t)
+            assert t.numel() == numel, (name, t.numel(), numel)
+            keep[name] = t
+            return t.data_ptr()
+
+        cb = WEIGHT_FN(get)
+        h = C.c_void_p()
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            check(self.lib.b2_lfm2_create(C.byref(d), cb, None, int(weights_on_host),
+                                          C.c_void_p(_stream_ptr(stream)), C.byref(h)),
+                  "b2_lfm2_create")
+        keep.clear()
+        self._h = h
+
+    def forward_gpu(self, ids: torch.Tensor, logits: torch.Tensor, batch: int, seq_len: int,
+                    stream: Optional[torch.cuda.Stream] = None, hidden_out=None) -> None:
+        assert ids.dtype == torch.int32 and ids.is_contiguous() and ids.is_cuda
+        fn = self.lib.b2_lfm2_forward_ex
+        check(fn(self._h, _vp(ids), batch, seq_len, _vp(logits), _vp(hidden_out),
+                 C.c_void_p(_stream_ptr(stream))), "b2_lfm2_forward")
+
+    def forward(self, ids: torch.Tensor, want_hidden: bool = False):
+        """ids [B, S] int -> logits [B, vocab] of each sequence's last position."""
+        B, S = ids.shape
+        ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+        logits = torch.empty(B, self.vocab, dtype=torch.float32, device=self.device)
+        hidden = (torch.empty(self.layers, B * S, self.H, dtype=torch.float32, device=self.device)
+                  if want_hidden else None)
+        self.forward_gpu(ids, logits, B, S, hidden_out=hidden)
+        return (logits, hidden) if want_hidden else logits
+
+    def device_status(self) -> int:
+        v = C.c_int(0)
+        rc = self.lib.b2_lfm2_get_status(self._h, C.c_void_p(_stream_ptr(None)), C.byref(v))
+        if rc not in (_lib.B2_OK, _lib.B2_ERR_DEVICE):
+            check(rc, "b2_lfm2_get_status")
+        return v.value
+
+    def device_bytes(self) -> int:
+        return int(self.lib.b2_lfm2_device_bytes(self._h))

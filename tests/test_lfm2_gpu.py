@@ -1,0 +1,185 @@
+"""Decoder glue and the whole model on the GPU, through the C ABI of
+include/b2lfm2.h, against the CPU oracle (itself pinned bit-exact to the
+reference's kernels by tests/test_lfm2_oracle.py) and the reference goldens.
+
+Bars:
+  * RMSNorm (fp32 in, fp32 out) and the rotary tables: bit-exact.
+  * attention / short-conv blocks (bf16 projections, fp32 accumulate):
+    max |got - ref| / max |ref| <= 1e-2, the bf16 bar of the MoE tests.
+  * a decoder layer of the model, fed the model's own previous residual: the
+    layer's update (output - input) within 1e-2 of the oracle's, per token
+    normalised by the update's max; MoE tokens whose oracle top-4 selection is
+    within 5e-3 of a tie are excluded (bf16 rounding of the projections may
+    legitimately flip them) and must be few.
+  * logits from the model's last residual: 1e-2; end to end against the
+    reference engine's logits for the same ids: 5e-3.
+"""
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as o
+import lfm2_cases as lc
+
+pytestmark = pytest.mark.gpu
+
+G = np.load(Path(__file__).parent / "golden" / "ref_lfm2.npz")
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _err(got, want):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    return float(np.abs(got - want).max() / np.abs(want).max())
+
+
+@pytest.fixture(scope="module")
+def W():
+    return lc.Weights(lc.MINI["seed"], lc.MINI["vocab"])
+
+
+def test_rmsnorm_bit_exact(cuda_dev):
+    from final_b200.lfm2 import rmsnorm
+    for tag, (rows, dim) in (("rms2048", (8, 2048)), ("rms64", (96, 64))):
+        x = o.randn((rows, dim), 31, dim, 3.0)
+        w = (o.randn((dim,), 31, dim + 1, 0.1) + np.float32(1.0)).astype(np.float32)
+        y = rmsnorm(_t(x, cuda_dev), _t(w, cuda_dev)).cpu().numpy()
+        assert np.array_equal(y, G[tag]), tag
+
+
+def test_add_rmsnorm_matches_add_then_norm(cuda_dev):
+    from final_b200 import _lib
+    lib = _lib.load()
+    r = o.randn((37, 2048), 32, 0, 1.0)
+    d = o.randn((37, 2048), 32, 1, 0.5)
+    w = (o.randn((2048,), 32, 2, 0.1) + np.float32(1.0)).astype(np.float32)
+    rt, dt, wt = _t(r, cuda_dev), _t(d, cuda_dev), _t(w, cuda_dev)
+    y32 = torch.empty(37, 2048, device=cuda_dev)
+    y16 = torch.empty(37, 2048, device=cuda_dev, dtype=torch.bfloat16)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.b2_add_rmsnorm(C.c_void_p(rt.data_ptr()), C.c_void_p(dt.data_ptr()),
+                                  C.c_void_p(wt.data_ptr()), C.c_void_p(y32.data_ptr()),
+                                  C.c_void_p(y16.data_ptr()), 37, 2048, 1e-5, s), "add_rmsnorm")
+    torch.cuda.synchronize()
+    want_r = (r + d).astype(np.float32)
+    assert np.array_equal(rt.cpu().numpy(), want_r)
+    want = o.rmsnorm(want_r, w)
+    assert np.array_equal(y32.cpu().numpy(), want)
+    assert torch.equal(y16.cpu(), torch.from_numpy(want).to(torch.bfloat16))
+
+
+def test_rope_tables_bit_exact():
+    import hashlib
+    from final_b200.lfm2 import rope_tables
+    c, s = rope_tables(4096)
+    assert hashlib.sha256(c.tobytes()).hexdigest() == str(G["rope_cos_sha256"])
+    assert hashlib.sha256(s.tobytes()).hexdigest() == str(G["rope_sin_sha256"])
+
+
+def test_embed(cuda_dev):
+    from final_b200.lfm2 import embed
+    table = o.randn((300, 64), 33, 0, 1.0)
+    ids = np.array([0, 299, 17, 17, 5], dtype=np.int32)
+    out = embed(_t(ids, cuda_dev), _t(table, cuda_dev)).cpu().numpy()
+    assert np.array_equal(out, table[ids])
+
+
+def _attn(W, dev, B, S, seed, stream):
+    from final_b200.lfm2 import Attention
+    pre = "layers.2.self_attn."
+    ws = [W(pre + n + ".weight") for n in ("q_proj", "k_proj", "v_proj", "out_proj",
+                                           "q_layernorm", "k_layernorm")]
+    x = o.randn((B * S, lc.H), seed, stream, 1.0)
+    c, s = o.rope_tables(S)
+    att = Attention(*[_t(a, dev) for a in ws], max_tokens=B * S)
+    y = att.forward(_t(x, dev), _t(c, dev), _t(s, dev), B, S)
+    torch.cuda.synchronize()
+    att.close()
+    return x, ws, c, s, y.cpu().numpy()
+
+
+def test_attention_block_golden(W, cuda_dev):
+    x, ws, c, s, y = _attn(W, cuda_dev, 2, 16, 41, 0)
+    rows = [0, 3, 7, 15, 16, 20, 27, 31]
+    assert _err(y[rows], G["attn_y_rows"]) < 1e-2
+
+
+@pytest.mark.parametrize("B,S", [(1, 1), (2, 70), (1, 200), (3, 129)])
+def test_attention_block_vs_oracle(W, cuda_dev, B, S):
+    x, ws, c, s, y = _attn(W, cuda_dev, B, S, 44, S)
+    want = o.attention_block(x, *ws, c, s, B, S)
+    assert _err(y, want) < 1e-2
+
+
+@pytest.mark.parametrize("B,S", [(2, 16), (1, 37), (3, 100), (1, 1)])
+def test_shortconv_block(W, cuda_dev, B, S):
+    from final_b200.lfm2 import ShortConv
+    pre = "layers.0.conv."
+    cw, iw, ow = W(pre + "conv.weight"), W(pre + "in_proj.weight"), W(pre + "out_proj.weight")
+    x = o.randn((B * S, lc.H), 42, S, 1.0)
+    conv = ShortConv(_t(cw, cuda_dev), _t(iw, cuda_dev), _t(ow, cuda_dev), max_tokens=B * S)
+    y = conv.forward(_t(x, cuda_dev), B, S).cpu().numpy()
+    conv.close()
+    want = o.shortconv_block(x, iw, cw, ow, B, S)
+    assert _err(y, want) < 1e-2
+    if (B, S) in ((2, 16), (1, 37)):
+        tag = "conv" if S == 16 else "conv37"
+        rows = [0, 3, 7, 15, 16, 20, 27, 31] if S == 16 else [0, 1, 2, 3, 17, 35, 36]
+        assert _err(y[rows], G[tag + "_y_rows"]) < 1e-2
+
+
+def _near_tie_tokens(W, i, hn, margin=5e-3):
+    """Tokens whose oracle top-4 score is within `margin` of the 5th."""
+    ff = f"layers.{i}.feed_forward."
+    logits = o.gemm_nt(hn, W(ff + "gate.weight"))
+    score = 1.0 / (1.0 + np.exp(-logits.astype(np.float64))) + W(ff + "expert_bias")
+    srt = np.sort(score, axis=1)[:, ::-1]
+    return np.where(srt[:, lc.K - 1] - srt[:, lc.K] < margin)[0]
+
+
+def test_mini_model(W, cuda_dev):
+    from final_b200.lfm2 import LFM2Model
+    B, S, L, V = lc.MINI["batch"], lc.MINI["seq"], lc.MINI["layers"], lc.MINI["vocab"]
+    model = LFM2Model(lambda name, n: W(name) if name != "lm_head.weight" else None,
+                      weights_on_host=True, max_batch=B, max_seq=S, num_layers=L, vocab=V)
+    ids = lc.token_ids(B, S, V, lc.MINI["seed"])
+    logits, hidden = model.forward(torch.from_numpy(ids), want_hidden=True)
+    torch.cuda.synchronize()
+    assert model.device_status() == 0
+    logits, hidden = logits.cpu().numpy(), hidden.cpu().numpy()
+    cos, sin = o.rope_tables(S)
+    x = W("embed_tokens.weight")[ids.reshape(-1)]
+    excluded = 0
+    for i in range(L):
+        want = lc.decoder_layer_oracle(W, i, x, B, S, cos, sin)
+        upd_got, upd_want = hidden[i] - x, want - x
+        keep = np.ones(B * S, dtype=bool)
+        if i >= lc.NUM_DENSE:
+            pre = f"layers.{i}."
+            h = x + lc.mixer_oracle(W, i, o.rmsnorm(x, W(pre + "operator_norm.weight")), B, S,
+                                    cos, sin)
+            near = _near_tie_tokens(W, i, o.rmsnorm(h, W(pre + "ffn_norm.weight")))
+            keep[near] = False
+            excluded += len(near)
+        err = np.abs(upd_got - upd_want).max(axis=1) / np.abs(upd_want).max(axis=1)
+        print(f"layer {i}: update err (kept tokens) {err[keep].max():.2e}, all {err.max():.2e}, "
+              f"near ties {int((~keep).sum())}")
+        assert err[keep].max() < 1e-2, (i, err.max())
+        x = hidden[i]
+        W.drop(f"layers.{i}.feed_forward.experts")
+    assert excluded <= B * S * (L - lc.NUM_DENSE) // 4
+    last = hidden[-1].reshape(B, S, lc.H)[:, -1, :]
+    want_logits = o.gemm_nt(o.rmsnorm(last, W("embedding_norm.weight")), W("embed_tokens.weight"))
+    print(f"logits vs oracle on the model's residual {_err(logits, want_logits):.2e}, "
+          f"vs reference golden {_err(logits, G['model_logits']):.2e}")
+    assert _err(logits, want_logits) < 1e-2
+    # end to end against the reference engine's own logits (golden): measured
+    # 6.9e-4 on a B200 with the bf16 projections of four layers compounded
+    assert _err(logits, G["model_logits"]) < 5e-3
+    model.close()
