@@ -53,6 +53,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-dense", action="store_true", help="skip the dense GEMM sweep")
+    p.add_argument("--no-model", action="store_true",
+                   help="skip the full-model forward (config 5)")
+    p.add_argument("--model-only", action="store_true",
+                   help="only time the full-model forward (config 5)")
     p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
                    help="expert placement when --gpus > 1")
     p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
@@ -425,6 +429,10 @@ def run_ours(args, rank, world, dev):
     if not args.no_dense and rank == 0:
         out["dense_gemm_sweep"] = dense_sweep(dev)
         out["dense_mlp"] = mlp_bench(dev)
+    if not args.no_model and rank == 0 and world == 1:
+        del layer
+        torch.cuda.empty_cache()
+        out["full_model"] = model_bench(dev)
     if w_host is not None:
         out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
     return out
@@ -542,6 +550,75 @@ def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
     mlp.close()
     if st:
         raise RuntimeError(f"MLP device status 0x{st:x}")
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------ model
+def model_bench(dev, B=32, S=512, steps=5, warmup=3):
+    """Config 5: the whole LFM2-8B-A1B-shaped model (24 layers, random-init
+    weights, vocab 65536) over batch 32 x seq 512 token ids uniform in
+    [0, 65536): samples/s of the last-token logits, device-timed with inputs
+    resident, and end to end with the ids copied from pinned host memory and
+    the logits copied back every step."""
+    import torch
+    from final_b200 import launch_count
+    from final_b200.lfm2 import LFM2Model, model_flop, synthetic_weights
+    t0 = time.time()
+    model = LFM2Model(synthetic_weights(dev, seed=11), max_batch=B, max_seq=S, device=dev)
+    torch.cuda.empty_cache()
+    build_s = time.time() - t0
+    g = torch.Generator(device=dev).manual_seed(12)
+    ids = torch.randint(0, 65536, (B, S), device=dev, generator=g, dtype=torch.int32)
+    logits = torch.empty(B, 65536, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        model.forward_gpu(ids, logits, B, S, stream)
+    torch.cuda.synchronize()
+    st = model.device_status()
+    if st:
+        raise RuntimeError(f"model device status 0x{st:x}")
+    sampler = ClockSampler(smi_index_for(dev.index))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    n0 = launch_count()
+    e0.record(stream)
+    for _ in range(steps):
+        model.forward_gpu(ids, logits, B, S, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n1 = launch_count()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / steps
+    # end to end: ids from pinned host memory, logits back to pinned host memory
+    ids_h = ids.cpu().pin_memory()
+    logits_h = torch.empty(B, 65536, dtype=torch.float32).pin_memory()
+    ids_d = torch.empty_like(ids)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        ids_d.copy_(ids_h, non_blocking=True)
+        model.forward_gpu(ids_d, logits, B, S, stream)
+        logits_h.copy_(logits, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1) / steps
+    st = model.device_status()
+    if st:
+        raise RuntimeError(f"model device status 0x{st:x}")
+    flop = model_flop(B, S)
+    pk = peaks()
+    out = {"workload": "lfm2_8b_a1b_shaped_forward", "batch": B, "seq_len": S, "layers": 24,
+           "vocab": 65536, "weights": "random init (bf16 projections / experts from fp32)",
+           "samples_per_s": B / (ms / 1e3), "tokens_per_s": B * S / (ms / 1e3),
+           "ms_per_forward": ms, "tflops": flop / (ms / 1e3) / 1e12,
+           "frac_of_bf16_peak": flop / (ms / 1e3) / 1e12 / pk["bf16"],
+           "flop_per_forward": flop, "gpu_launches_per_forward": int(n1 - n0) // steps,
+           "e2e": {"samples_per_s": B / (ems / 1e3), "ms_per_step": ems,
+                   "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": B * 65536 * 4},
+           "device_bytes": model.device_bytes(), "build_s": build_s, "clocks": clocks,
+           "steps": steps, "warmup": warmup}
+    model.close()
     torch.cuda.empty_cache()
     return out
 
@@ -687,6 +764,9 @@ def main():
                                 device_id=dev)
     if args.gemm:
         print(json.dumps(gemm_only(args, dev)), flush=True)
+        return 0
+    if args.model_only:
+        print(json.dumps(model_bench(dev, steps=args.steps, warmup=args.warmup)), flush=True)
         return 0
     try:
         out = run_ours(args, rank, world, dev)

@@ -232,3 +232,51 @@ class LFM2Model(_Handle):
 
     def device_bytes(self) -> int:
         return int(self.lib.b2_lfm2_device_bytes(self._h))
+
+
+def synthetic_weights(device, seed: int = 0):
+    """Random-init weights of the reference architecture, by tensor name, as
+    fp32 tensors on `device`: embedding N(0,1); RMSNorm weights N(1,0.1);
+    conv taps N(0,0.3); projections, experts, router and expert bias
+    N(0,0.02); no separate lm_head.weight (tied, as the reference model).
+    For benchmarks: no checkpoint is needed."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def get(name: str, numel: int):
+        if name == "lm_head.weight":
+            return None
+        last = name.split(".")[-2] if name.count(".") else name
+        if name == "embed_tokens.weight":
+            mean, std = 0.0, 1.0
+        elif "norm" in last:
+            mean, std = 1.0, 0.1
+        elif name.endswith("conv.conv.weight"):
+            mean, std = 0.0, 0.3
+        else:
+            mean, std = 0.0, 0.02
+        return torch.empty(numel, dtype=torch.float32, device=device).normal_(mean, std,
+                                                                              generator=g)
+    return get
+
+
+def model_flop(batch: int, seq: int, cfg=None, layer_types=LAYER_TYPES) -> float:
+    """Algorithmic FLOP of one forward (2 per multiply-add): projections,
+    causal attention core, dense MLP / MoE experts and router, last-token LM
+    head; elementwise work not counted."""
+    c = dict(CONFIG)
+    c.update(cfg or {})
+    H, Hq, Hkv = c["hidden"], c["num_heads"], c["num_kv_heads"]
+    T = batch * seq
+    f = 0.0
+    for i in range(c["num_layers"]):
+        if layer_types[i] == 0:
+            f += T * 2.0 * H * (Hq + 2 * Hkv) * 64 + T * 2.0 * Hq * 64 * H
+            f += batch * 4.0 * Hq * 64 * seq * (seq + 1) / 2
+        else:
+            f += T * 2.0 * H * 3 * H + T * 2.0 * H * H
+        if i < c["num_dense_layers"]:
+            f += T * 6.0 * H * c["dense_inter"]
+        else:
+            f += T * (2.0 * H * c["num_experts"] + c["top_k"] * 6.0 * H * c["moe_inter"])
+    return f + batch * 2.0 * H * c["vocab"]
