@@ -31,6 +31,9 @@ EXPORTED = (
     "b2_conv_create", "b2_conv_forward", "b2_conv_destroy",
     "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex", "b2_lfm2_get_status",
     "b2_lfm2_device_bytes", "b2_lfm2_destroy",
+    # include/b2loader.h
+    "b2_loader_open", "b2_loader_num_tensors", "b2_loader_name", "b2_loader_tensor",
+    "b2_loader_weight", "b2_loader_close",
 )
 
 EP_MAX_WORLD = 64
@@ -169,6 +172,19 @@ def load(path: Path | None = None):
                  "b2_conv_destroy", "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex",
                  "b2_lfm2_get_status", "b2_lfm2_destroy"):
         getattr(lib, name).restype = i
+    lib.b2_loader_open.argtypes = [C.c_char_p, C.POINTER(vp)]
+    lib.b2_loader_open.restype = i
+    lib.b2_loader_num_tensors.argtypes = [vp]
+    lib.b2_loader_num_tensors.restype = C.c_int64
+    lib.b2_loader_name.argtypes = [vp, C.c_int64]
+    lib.b2_loader_name.restype = C.c_char_p
+    lib.b2_loader_tensor.argtypes = [vp, C.c_char_p, C.POINTER(vp), C.POINTER(C.c_int64),
+                                     C.POINTER(C.c_int64), C.POINTER(i)]
+    lib.b2_loader_tensor.restype = i
+    lib.b2_loader_weight.argtypes = [vp, C.c_char_p, C.c_int64]
+    lib.b2_loader_weight.restype = vp
+    lib.b2_loader_close.argtypes = [vp]
+    lib.b2_loader_close.restype = i
     lib.b2_kernel_launch_count.restype = C.c_uint64
     lib.b2_moe_tile_rows.restype = i
     lib.b2_status_string.argtypes = [i]

@@ -23,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
 
-SOURCES = ["b2moe_api.cu", "ep.cu", "noalloc.cu", "mlp.cu", "lfm2.cu"]
+SOURCES = ["b2moe_api.cu", "ep.cu", "noalloc.cu", "mlp.cu", "lfm2.cu", "loader.cpp"]
 
 
 def _needs_rebuild(target: Path, deps) -> bool:
@@ -35,7 +35,8 @@ def _needs_rebuild(target: Path, deps) -> bool:
 
 def _deps():
     out = []
-    for p in list(CSRC.rglob("*.cu")) + list(CSRC.rglob("*.cuh")) + list(CSRC.rglob("*.h")):
+    for p in (list(CSRC.rglob("*.cu")) + list(CSRC.rglob("*.cuh")) + list(CSRC.rglob("*.h")) +
+              list(CSRC.rglob("*.cpp"))):
         out.append(p)
     out += list((ROOT / "include").glob("*.h"))
     return out

@@ -1,21 +1,27 @@
-// b2_layers_run.cpp -- drives the C++ drop-in layers the way the reference's
-// DecoderLayer::forward_gpu does (src/layer.cu:1908-1914): construct by layer
-// index / tensor names, init_gpu(), forward_gpu() on device fp32 buffers.
-// Used by the parity tests to exercise the C++ boundary end to end.
+// b2_layers_run.cpp -- drives the C++ drop-in classes the way the reference
+// engine drives its own (construct by layer index / tensor names, init_gpu(),
+// forward_gpu() on device fp32 buffers; DecoderLayer::forward_gpu,
+// src/layer.cu:1895-1919; LFM2Model::forward + sync, src/main.cpp).  The
+// parity tests use it to exercise the C++ boundary end to end.
 //
-//   b2_layers_run moe <weights_dir> <layer_idx> <tokens> <x.f32> <y.f32> [bf16|tf32]
-//   b2_layers_run mlp <weights_dir> <layer_idx> <tokens> <x.f32> <y.f32> [bf16|tf32]
+//   b2_layers_run moe     <weights> <layer> <tokens> <x.f32> <y.f32> [bf16|tf32]
+//   b2_layers_run mlp     <weights> <layer> <tokens> <x.f32> <y.f32> [bf16|tf32]
+//   b2_layers_run attn    <weights> <layer> <batch> <seq> <x.f32> <y.f32>
+//   b2_layers_run conv    <weights> <layer> <batch> <seq> <x.f32> <y.f32>
+//   b2_layers_run decoder <weights> <layer> <is_attention> <batch> <seq> <x.f32> <y.f32>
+//   b2_layers_run model   <model.bin> <batch> <seq> <ids.i32> <logits.f32>
 //
-// Weights come from a DirWeightStore over <weights_dir> under the reference's
-// tensor names; x is read from <x.f32> ([tokens][2048-or-stored hidden] fp32)
-// and y written to <y.f32>.
+// <weights> is a directory of <name>.f32 / <name>.shape files or a model file
+// in the reference's format.  x is [tokens][hidden] fp32; y the same.
 #include <cuda_runtime.h>
 
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <memory>
 #include <string>
+#include <sys/stat.h>
 #include <vector>
 
 #include "b2_layers.h"
@@ -32,8 +38,57 @@
 
 static void usage() {
   fprintf(stderr,
-          "usage: b2_layers_run <moe|mlp> <weights_dir> <layer_idx> <tokens> <x.f32> <y.f32> "
-          "[bf16|tf32]\n");
+          "usage: b2_layers_run moe|mlp <weights> <layer> <tokens> <x.f32> <y.f32> [bf16|tf32]\n"
+          "       b2_layers_run attn|conv <weights> <layer> <batch> <seq> <x.f32> <y.f32>\n"
+          "       b2_layers_run decoder <weights> <layer> <is_attention> <batch> <seq> <x.f32> "
+          "<y.f32>\n"
+          "       b2_layers_run model <model.bin> <batch> <seq> <ids.i32> <logits.f32>\n");
+}
+
+template <typename T>
+static bool read_file(const char *path, std::vector<T> *v) {
+  std::ifstream f(path, std::ios::binary);
+  f.read(reinterpret_cast<char *>(v->data()), (std::streamsize)(v->size() * sizeof(T)));
+  return (size_t)f.gcount() == v->size() * sizeof(T);
+}
+
+template <typename T>
+static void write_file(const char *path, const std::vector<T> &v) {
+  std::ofstream f(path, std::ios::binary);
+  f.write(reinterpret_cast<const char *>(v.data()), (std::streamsize)(v.size() * sizeof(T)));
+}
+
+static std::unique_ptr<b2layer::WeightStore> open_store(const std::string &src) {
+  struct stat st;
+  if (stat(src.c_str(), &st) == 0 && S_ISDIR(st.st_mode))
+    return std::unique_ptr<b2layer::WeightStore>(new b2layer::DirWeightStore(src));
+  return std::unique_ptr<b2layer::WeightStore>(new b2layer::ModelLoader(src));
+}
+
+static int run_model(int argc, char **argv) {
+  if (argc < 7) {
+    usage();
+    return 2;
+  }
+  const int B = atoi(argv[3]), S = atoi(argv[4]);
+  b2layer::set_model_limits(B, S);
+  b2layer::LFM2Model model(argv[2]);
+  std::vector<int> ids((size_t)B * S);
+  if (!read_file(argv[5], &ids)) {
+    fprintf(stderr, "short read of %s\n", argv[5]);
+    return 1;
+  }
+  std::vector<float> logits((size_t)B * model.vocab()), again(logits.size());
+  model.forward(0, B, ids.data(), S, logits.data());
+  model.forward(B, B, ids.data(), S, again.data());  // the next batch slot (next replica)
+  model.sync();
+  if (memcmp(logits.data(), again.data(), logits.size() * sizeof(float)) != 0) {
+    fprintf(stderr, "two forwards of the same ids differ\n");
+    return 1;
+  }
+  write_file(argv[6], logits);
+  printf("ok model B=%d S=%d V=%d\n", B, S, model.vocab());
+  return 0;
 }
 
 int main(int argc, char **argv) {
@@ -41,43 +96,83 @@ int main(int argc, char **argv) {
     usage();
     return 0;
   }
-  if (argc < 7) {
+  if (argc < 2) {
     usage();
     return 2;
   }
-  const std::string kind = argv[1], dir = argv[2];
-  const int layer = atoi(argv[3]), T = atoi(argv[4]);
-  const int dtype = (argc > 7 && !strcmp(argv[7], "tf32")) ? B2_TF32 : B2_BF16;
-  b2layer::DirWeightStore store(dir);
-  b2layer::set_weight_store(&store);
+  const std::string kind = argv[1];
+  if (kind == "model") return run_model(argc, argv);
+  const bool seq_form = kind == "attn" || kind == "conv" || kind == "decoder";
+  const int need = kind == "decoder" ? 9 : seq_form ? 8 : 7;
+  if (argc < need) {
+    usage();
+    return 2;
+  }
+  std::unique_ptr<b2layer::WeightStore> store = open_store(argv[2]);
+  b2layer::set_weight_store(store.get());
+  const int layer = atoi(argv[3]);
+  int a = 4;
+  const bool is_attn = kind == "decoder" ? atoi(argv[a++]) != 0 : kind == "attn";
+  int B = 1, S = 0;
+  if (seq_form) {
+    B = atoi(argv[a++]);
+    S = atoi(argv[a++]);
+  } else {
+    S = atoi(argv[a++]);
+  }
+  const char *xin = argv[a++], *yout = argv[a++];
+  const int T = B * S;
+  const int dtype = (!seq_form && argc > 7 && !strcmp(argv[7], "tf32")) ? B2_TF32 : B2_BF16;
   b2layer::set_max_tokens(T > 0 ? T : 1);
   b2layer::set_gemm_dtype(dtype);
 
-  const std::string pre = "layers." + std::to_string(layer) + ".feed_forward.";
-  b2layer::SparseMoeBlock *moe = nullptr;
-  b2layer::MLP *mlp = nullptr;
+  const std::string pre = "layers." + std::to_string(layer) + ".";
   int H = 0;
+  {
+    std::vector<float> d;
+    std::vector<size_t> s;
+    const std::string probe = kind == "moe" ? pre + "feed_forward.gate.weight"
+                              : kind == "mlp" ? pre + "feed_forward.w1.weight"
+                                              : pre + "operator_norm.weight";
+    if (!store->load(probe, &d, &s)) {
+      fprintf(stderr, "missing tensor %s\n", probe.c_str());
+      return 1;
+    }
+    H = (int)s.back();
+  }
+  std::unique_ptr<b2layer::SparseMoeBlock> moe;
+  std::unique_ptr<b2layer::MLP> mlp;
+  std::unique_ptr<b2layer::Attention> att;
+  std::unique_ptr<b2layer::ShortConv> conv;
+  std::unique_ptr<b2layer::DecoderLayer> dec;
+  std::unique_ptr<b2layer::RotaryEmbedding> rope;
   if (kind == "moe") {
-    moe = new b2layer::SparseMoeBlock(layer);
+    moe.reset(new b2layer::SparseMoeBlock(layer));
     moe->init_gpu();
   } else if (kind == "mlp") {
-    mlp = new b2layer::MLP(pre + "w1.weight", pre + "w2.weight", pre + "w3.weight");
+    const std::string ff = pre + "feed_forward.";
+    mlp.reset(new b2layer::MLP(ff + "w1.weight", ff + "w2.weight", ff + "w3.weight"));
     mlp->init_gpu();
+  } else if (kind == "attn") {
+    att.reset(new b2layer::Attention(layer));
+    att->init_gpu();
+  } else if (kind == "conv") {
+    conv.reset(new b2layer::ShortConv(layer));
+    conv->init_gpu();
+  } else if (kind == "decoder") {
+    dec.reset(new b2layer::DecoderLayer(layer, is_attn));
+    dec->init_gpu(0);
   } else {
     usage();
     return 2;
   }
-  {
-    std::vector<float> d;
-    std::vector<size_t> s;
-    store.load(kind == "moe" ? pre + "gate.weight" : pre + "w1.weight", &d, &s);
-    H = (int)s[1];
+  if (is_attn) {
+    rope.reset(new b2layer::RotaryEmbedding());
+    rope->init_gpu();
   }
   std::vector<float> x((size_t)T * H), y((size_t)T * H);
-  std::ifstream fx(argv[5], std::ios::binary);
-  fx.read(reinterpret_cast<char *>(x.data()), (std::streamsize)(x.size() * 4));
-  if ((size_t)fx.gcount() != x.size() * 4) {
-    fprintf(stderr, "short read of %s\n", argv[5]);
+  if (!read_file(xin, &x)) {
+    fprintf(stderr, "short read of %s\n", xin);
     return 1;
   }
   float *dx = nullptr, *dy = nullptr;
@@ -88,6 +183,10 @@ int main(int argc, char **argv) {
   RUN_CHECK(cudaMemcpyAsync(dx, x.data(), x.size() * 4, cudaMemcpyHostToDevice, st));
   if (moe) moe->forward_gpu(dx, dy, 1, T, H, st);
   if (mlp) mlp->forward_gpu(dx, dy, 1, T, H, st);
+  if (att) att->forward_gpu(dx, rope->cos_gpu_, rope->sin_gpu_, dy, B, S, H, st);
+  if (conv) conv->forward_gpu(dx, dy, B, S, H, st);
+  if (dec) dec->forward_gpu(dx, rope ? rope->cos_gpu_ : nullptr, rope ? rope->sin_gpu_ : nullptr,
+                            dy, B, S, H, st);
   RUN_CHECK(cudaMemcpyAsync(y.data(), dy, y.size() * 4, cudaMemcpyDeviceToHost, st));
   RUN_CHECK(cudaStreamSynchronize(st));
   int dev_status = 0;
@@ -99,13 +198,10 @@ int main(int argc, char **argv) {
     fprintf(stderr, "device status 0x%x\n", dev_status);
     return 1;
   }
-  std::ofstream fy(argv[6], std::ios::binary);
-  fy.write(reinterpret_cast<const char *>(y.data()), (std::streamsize)(y.size() * 4));
-  delete moe;
-  delete mlp;
+  write_file(yout, y);
   cudaFree(dx);
   cudaFree(dy);
   cudaStreamDestroy(st);
-  printf("ok %s T=%d H=%d\n", kind.c_str(), T, H);
+  printf("ok %s B=%d S=%d H=%d\n", kind.c_str(), B, S, H);
   return 0;
 }

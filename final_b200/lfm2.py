@@ -196,15 +196,37 @@ class LFM2Model(_Handle):
             keep[name] = t
             return t.data_ptr()
 
-        cb = WEIGHT_FN(get)
+        from .modelfile import ModelFile
+        if isinstance(weights, ModelFile):
+            # straight from the memory-mapped file: the C loader is the source
+            cb, ctx, weights_on_host = C.cast(self.lib.b2_loader_weight, WEIGHT_FN), \
+                weights.handle, True
+        else:
+            cb, ctx = WEIGHT_FN(get), None
         h = C.c_void_p()
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         with torch.cuda.device(self.device):
-            check(self.lib.b2_lfm2_create(C.byref(d), cb, None, int(weights_on_host),
+            check(self.lib.b2_lfm2_create(C.byref(d), cb, ctx, int(weights_on_host),
                                           C.c_void_p(_stream_ptr(stream)), C.byref(h)),
                   "b2_lfm2_create")
         keep.clear()
         self._h = h
+
+    @classmethod
+    def from_file(cls, path: str, *, max_batch: int, max_seq: int, dtype: str = "bf16",
+                  device: Optional[torch.device] = None, **overrides) -> "LFM2Model":
+        """Load a model file in the reference's format (final_b200.modelfile);
+        the configuration is inferred from its tensors."""
+        from .modelfile import ModelFile
+        mf = ModelFile(path)
+        try:
+            cfg = mf.config()
+            cfg.update(overrides)
+            types = cfg.pop("layer_types")
+            return cls(mf, max_batch=max_batch, max_seq=max_seq, layer_types=types,
+                       dtype=dtype, device=device, **cfg)
+        finally:
+            mf.close()
 
     def forward_gpu(self, ids: torch.Tensor, logits: torch.Tensor, batch: int, seq_len: int,
                     stream: Optional[torch.cuda.Stream] = None, hidden_out=None) -> None:

@@ -29,13 +29,22 @@ THETA = 1000000.0
 # vocabulary, small enough for the CPU oracle.
 MINI = dict(layers=4, vocab=1024, batch=2, seq=16, seed=21)
 
+# Shapes of a model: the reference's, and a tiny one (model-file and C++
+# class tests, where the whole model is written to disk).
+REF = dict(H=H, HQ=HQ, HKV=HKV, E=E, K=K, I_MOE=I_MOE, I_DENSE=I_DENSE, NUM_DENSE=NUM_DENSE,
+           TYPES=LAYER_TYPES)
+TINY = dict(H=256, HQ=4, HKV=2, E=8, K=4, I_MOE=128, I_DENSE=384, NUM_DENSE=2,
+            TYPES=(1, 1, 0, 1, 0), layers=5, vocab=300, batch=3, seq=23, seed=22)
+
 
 def stream_of(name: str) -> int:
     return zlib.crc32(name.encode()) & 0xFFFFFFFF
 
 
-def weight_spec(name: str, vocab: int):
+def weight_spec(name: str, vocab: int, cfg=REF):
     """(shape, mean, std) of a tensor by its reference name."""
+    H, HQ, HKV, E = cfg["H"], cfg["HQ"], cfg["HKV"], cfg["E"]
+    I_MOE, I_DENSE = cfg["I_MOE"], cfg["I_DENSE"]
     p = name.split(".")
     if name == "embed_tokens.weight":
         return (vocab, H), 0.0, 1.0
@@ -64,12 +73,12 @@ def weight_spec(name: str, vocab: int):
 class Weights:
     """Lazily generated, cached tensors by reference name."""
 
-    def __init__(self, seed: int, vocab: int):
-        self.seed, self.vocab, self.cache = seed, vocab, {}
+    def __init__(self, seed: int, vocab: int, cfg=REF):
+        self.seed, self.vocab, self.cache, self.cfg = seed, vocab, {}, cfg
 
     def __call__(self, name: str) -> np.ndarray:
         if name not in self.cache:
-            shape, mean, std = weight_spec(name, self.vocab)
+            shape, mean, std = weight_spec(name, self.vocab, self.cfg)
             a = o.randn(shape, self.seed, stream_of(name), std)
             if mean:
                 a = (a + np.float32(mean)).astype(np.float32)
@@ -81,7 +90,8 @@ class Weights:
             del self.cache[k]
 
 
-def layer_names(i: int, is_attention: bool, vocab: int = 0):
+def layer_names(i: int, is_attention: bool, cfg=REF):
+    E, NUM_DENSE = cfg["E"], cfg["NUM_DENSE"]
     pre = f"layers.{i}."
     names = [pre + "operator_norm.weight", pre + "ffn_norm.weight"]
     if is_attention:
@@ -98,7 +108,16 @@ def layer_names(i: int, is_attention: bool, vocab: int = 0):
     return names
 
 
+def model_names(layers: int, cfg=REF):
+    """Every tensor name of a model with `layers` layers (tied LM head)."""
+    names = ["embed_tokens.weight", "embedding_norm.weight"]
+    for i in range(layers):
+        names += layer_names(i, cfg["TYPES"][i] == 0, cfg)
+    return names
+
+
 def experts(W: Weights, i: int):
+    E = W.cfg["E"]
     pre = f"layers.{i}.feed_forward."
     w1 = np.stack([W(pre + f"experts.{e}.w1.weight") for e in range(E)])
     w2 = np.stack([W(pre + f"experts.{e}.w2.weight") for e in range(E)])
@@ -109,7 +128,7 @@ def experts(W: Weights, i: int):
 def mixer_oracle(W: Weights, i: int, xn: np.ndarray, B: int, S: int, cos, sin):
     """The layer's attention or short-conv block on its normed input."""
     pre = f"layers.{i}."
-    if LAYER_TYPES[i] == 0:
+    if W.cfg["TYPES"][i] == 0:
         return o.attention_block(xn, W(pre + "self_attn.q_proj.weight"),
                                  W(pre + "self_attn.k_proj.weight"),
                                  W(pre + "self_attn.v_proj.weight"),
@@ -122,10 +141,11 @@ def mixer_oracle(W: Weights, i: int, xn: np.ndarray, B: int, S: int, cos, sin):
 
 def ffn_oracle(W: Weights, i: int, hn: np.ndarray):
     pre = f"layers.{i}.feed_forward."
-    if i < NUM_DENSE:
+    if i < W.cfg["NUM_DENSE"]:
         return o.dense_mlp(hn, W(pre + "w1.weight"), W(pre + "w3.weight"), W(pre + "w2.weight"))
     w1, w2, w3 = experts(W, i)
-    return o.moe_forward(hn, W(pre + "gate.weight"), W(pre + "expert_bias"), w1, w2, w3, K=K)["y"]
+    return o.moe_forward(hn, W(pre + "gate.weight"), W(pre + "expert_bias"), w1, w2, w3,
+                         K=W.cfg["K"])["y"]
 
 
 def decoder_layer_oracle(W: Weights, i: int, x: np.ndarray, B: int, S: int, cos, sin):
@@ -147,6 +167,7 @@ def model_oracle(W: Weights, ids: np.ndarray, layers: int, want_hidden=False):
     token and the LM head (src/model.cu:404-548, tied weights when the model
     has no lm_head.weight, src/model.cu:172-179)."""
     B, S = ids.shape
+    H = W.cfg["H"]
     cos, sin = o.rope_tables(S)
     x = W("embed_tokens.weight")[ids.reshape(-1)].astype(np.float32)
     hidden = []

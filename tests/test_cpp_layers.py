@@ -84,3 +84,79 @@ def test_cpp_mlp(cuda_dev, oracle, tmp_path, dtype):
         _store(tmp_path, f"{pre}{n}.weight", a)
     y = _run("mlp", tmp_path, layer, x, dtype)
     assert _rel(y, oracle.dense_mlp(x, w1, w3, w2)) < TOL[dtype]
+
+
+# ---------------------------------------------------------------- decoder
+# The rest of the reference's classes (Attention, ShortConv, DecoderLayer,
+# LFM2Model with its ModelLoader) over a tiny model written in the
+# reference's file format: weights under the reference's names, read by the
+# C++ ModelLoader, results against the CPU oracle.
+import lfm2_cases as lc  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def tiny_file(tmp_path_factory):
+    from final_b200.modelfile import write
+    cfg = lc.TINY
+    W = lc.Weights(cfg["seed"], cfg["vocab"], cfg)
+    p = tmp_path_factory.mktemp("tiny") / "tiny.bin"
+    write(str(p), {n: W(n) for n in lc.model_names(cfg["layers"], cfg)})
+    return p, W
+
+
+def _run_seq(kind, src, layer, B, S, x, extra=()):
+    d = Path(str(src)).parent
+    xf, yf = d / f"x_{kind}_{layer}.f32", d / f"y_{kind}_{layer}.f32"
+    xf.write_bytes(np.ascontiguousarray(x, dtype=np.float32).tobytes())
+    r = subprocess.run([str(RUN), kind, str(src), str(layer), *[str(e) for e in extra], str(B),
+                        str(S), str(xf), str(yf)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return np.frombuffer(yf.read_bytes(), dtype=np.float32).reshape(x.shape)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,layer", [("attn", 2), ("conv", 0)])
+def test_cpp_attention_and_shortconv(cuda_dev, oracle, tiny_file, kind, layer):
+    _built()
+    p, W = tiny_file
+    B, S, H = 2, 37, lc.TINY["H"]
+    x = oracle.randn((B * S, H), 50, layer, 1.0)
+    y = _run_seq(kind, p, layer, B, S, x)
+    c, s = oracle.rope_tables(S)
+    want = lc.mixer_oracle(W, layer, x, B, S, c, s)
+    assert _rel(y, want) < 1e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layer", [0, 2, 3])
+def test_cpp_decoder_layer(cuda_dev, oracle, tiny_file, layer):
+    _built()
+    p, W = tiny_file
+    B, S, H = 3, 23, lc.TINY["H"]
+    x = oracle.randn((B * S, H), 51, layer, 1.0)
+    is_attn = int(lc.TINY["TYPES"][layer] == 0)
+    y = _run_seq("decoder", p, layer, B, S, x, extra=(is_attn,))
+    c, s = oracle.rope_tables(S)
+    want = lc.decoder_layer_oracle(W, layer, x, B, S, c, s)
+    # the layer's update (output - input), per token
+    err = np.abs((y - x) - (want - x)).max(axis=1) / np.abs(want - x).max(axis=1)
+    assert np.sort(err)[-2] < 1e-2, err.max()   # at most one token may flip a near-tie expert
+
+
+@pytest.mark.gpu
+def test_cpp_model_from_file(cuda_dev, tiny_file, tmp_path):
+    """LFM2Model(model_file) + forward + sync as the reference's main drives it."""
+    _built()
+    p, W = tiny_file
+    cfg = lc.TINY
+    B, S = cfg["batch"], cfg["seq"]
+    ids = lc.token_ids(B, S, cfg["vocab"], cfg["seed"])
+    idf, lf = tmp_path / "ids.i32", tmp_path / "logits.f32"
+    idf.write_bytes(ids.astype(np.int32).tobytes())
+    r = subprocess.run([str(RUN), "model", str(p), str(B), str(S), str(idf), str(lf)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    logits = np.frombuffer(lf.read_bytes(), dtype=np.float32).reshape(B, cfg["vocab"])
+    want = lc.model_oracle(W, ids, cfg["layers"])
+    print(f"C++ LFM2Model logits vs oracle: {_rel(logits, want):.2e}")
+    assert _rel(logits, want) < 5e-3  # measured 5.5e-4 on a B200
