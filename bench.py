@@ -59,6 +59,8 @@ def parse():
                    help="only time the full-model forward (config 5)")
     p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
                    help="expert placement when --gpus > 1")
+    p.add_argument("--gemm-configs", type=int, nargs=3, metavar=("M", "N", "K"),
+                   help="time every dense-GEMM kernel configuration on one shape (bf16)")
     p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
                    help="only time b2_gemm_nt on one dense shape (bf16 operands), "
                         "e.g. for a profiler capture of the dense kernel")
@@ -519,6 +521,51 @@ def gemm_only(args, dev):
             "warmup": args.warmup}
 
 
+def gemm_configs(args, dev, reps=20):
+    """Every kernel configuration of b2_gemm_nt_config on one shape: device
+    time per call (CUDA-graph replay of `reps` calls, so launch overhead of
+    the host is not measured) and the error against fp64."""
+    import torch
+    from final_b200 import gemm_nt, to_bf16
+    from final_b200.moe import gemm_plan
+    M, N, Kd = args.gemm_configs
+    g = torch.Generator(device=dev).manual_seed(2)
+    A = to_bf16(torch.randn(M, Kd, device=dev, generator=g))
+    B = to_bf16(torch.randn(N, Kd, device=dev, generator=g) * 0.02)
+    C = torch.empty(M, N, device=dev)
+    ref = A.double() @ B.double().T
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    cfgs = ([("single", bn, 1) for bn in (64, 128, 256)] + [("pair", 256, 1)] +
+            [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)])
+    res = {"metric": "dense_gemm_configs", "M": M, "N": N, "K": Kd,
+           "plan": list(gemm_plan(M, N, Kd, "bf16", sms)), "us": {}}
+    for cfg in cfgs:
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            try:
+                gemm_nt(A, B, out=C, config=cfg, stream=s)
+            except Exception:
+                continue
+            s.synchronize()
+            err = ((C.double() - ref).abs().max() / ref.abs().max()).item()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                for _ in range(reps):
+                    gemm_nt(A, B, out=C, config=cfg, stream=s)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res["us"]["/".join(map(str, cfg))] = [round(e0.elapsed_time(e1) / (5 * reps) * 1e3, 2),
+                                              err]
+    return res
+
+
 def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
     """Dense SwiGLU MLP of the layers without experts (I = 7168) over T tokens
     on the same GEMM core: tokens/s and TFLOP/s (6*T*H*I FLOP per forward)."""
@@ -764,6 +811,9 @@ def main():
                                 device_id=dev)
     if args.gemm:
         print(json.dumps(gemm_only(args, dev)), flush=True)
+        return 0
+    if args.gemm_configs:
+        print(json.dumps(gemm_configs(args, dev)), flush=True)
         return 0
     if args.model_only:
         print(json.dumps(model_bench(dev, steps=args.steps, warmup=args.warmup)), flush=True)

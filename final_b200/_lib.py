@@ -18,6 +18,7 @@ B2_BF16, B2_TF32, B2_F32 = 0, 1, 2
 EXPORTED = (
     "b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
     "b2_moe_get_status", "b2_moe_tile_rows", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
+    "b2_gemm_plan", "b2_gemm_nt_config",
     "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
@@ -130,6 +131,10 @@ def load(path: Path | None = None):
     lib.b2_moe_device_bytes.restype = sz
     lib.b2_gemm_nt.argtypes = [vp, vp, vp, i, i, i, i, i, vp, vp]
     lib.b2_convert_f32_to_bf16.argtypes = [vp, vp, sz, vp]
+    lib.b2_gemm_plan.argtypes = [i, i, i, i, i, C.POINTER(i), C.POINTER(i), C.POINTER(i)]
+    lib.b2_gemm_plan.restype = i
+    lib.b2_gemm_nt_config.argtypes = [vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp]
+    lib.b2_gemm_nt_config.restype = i
     lib.b2_moe_route_noalloc.argtypes = [vp, vp, vp, i, i, i, i, C.c_float, vp, vp, vp, vp, vp, vp]
     lib.b2_ep_plan_compute.argtypes = [i, i, i, i, vp, C.POINTER(EpPlan)]
     lib.b2_ep_unique_id.argtypes = [vp]

@@ -23,6 +23,57 @@ std::atomic<uint64_t> &launch_counter() {
   return n;
 }
 
+namespace {
+template <typename Kern>
+void query_caps(Kern kern, size_t smem, int sms, int *caps) {
+  for (int sp = 0; sp <= kSplitMax; ++sp) caps[sp] = sp >= 2 ? static_max_clusters(sms, sp) : 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  for (int sp = 2; sp <= kSplitMax; ++sp) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sp * 64);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = sp;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0)
+      caps[sp] = n;
+    else
+      cudaGetLastError();
+  }
+}
+}  // namespace
+
+const int *splitk_cluster_caps(bool swiglu_width) {
+  // [device ordinal < 16][bn 128 / 256][size]
+  static int caps[16][2][kSplitMax + 1];
+  static std::atomic<uint32_t> done[16];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DevInfo di;
+  if (dev < 0 || dev >= 16 || !dev_info(&di)) return nullptr;
+  const int w = swiglu_width ? 1 : 0;
+  if (!(done[dev].load(std::memory_order_acquire) & (1u << w))) {
+    if (w)
+      query_caps(gemm_splitk_kernel<kEpiStore, false, float, 256>, splitk_smem_bytes(256), di.sms,
+                 caps[dev][w]);
+    else
+      query_caps(gemm_splitk_kernel<kEpiStore, false, float, 128>, splitk_smem_bytes(128), di.sms,
+                 caps[dev][w]);
+    done[dev].fetch_or(1u << w, std::memory_order_acq_rel);
+  }
+  return caps[dev][w];
+}
+
 static cudaEvent_t prof_event(b2_moe *m) {
   if (!m->ev_pool.empty()) {
     cudaEvent_t e = m->ev_pool.back();
@@ -400,8 +451,10 @@ extern "C" b2_status b2_moe_profile_read(b2_moe *m, float *stage_ms, int *forwar
 extern "C" size_t b2_moe_device_bytes(const b2_moe *m) { return m ? m->bytes : 0; }
 
 // ---------------------------------------------------------------- dense GEMM
-extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, int N, int K,
-                                int ldc, int dtype, int *status, b2_stream stream_) {
+// b2_gemm_nt with the plan given (kind < 0: the planner's choice).
+static b2_status gemm_nt_impl(const void *A, const void *B, float *C, int M, int N, int K, int ldc,
+                              int dtype, int kind, int bn, int split, int *status,
+                              b2_stream stream_) {
   if (M < 0 || N <= 0 || K <= 0 || ldc < N || (M > 0 && (!A || !B || !C)))
     return B2_ERR_INVALID;
   if (dtype != B2_BF16 && dtype != B2_TF32) return B2_ERR_INVALID;
@@ -411,7 +464,20 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
   DevInfo di;
   if (!dev_info(&di)) return B2_ERR_NO_DEVICE;
   const size_t es = f ? 4 : 2;
-  const DensePlan plan = plan_dense(M, N, di.sms, false);
+  const int kblocks = (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes);
+  DensePlan plan = plan_dense(M, N, di.sms, false, kblocks, splitk_cluster_caps(false));
+  if (kind == 0) {
+    if (bn != 64 && bn != 128 && bn != 256) return B2_ERR_INVALID;
+    plan = {false, bn, bn, 1};
+  } else if (kind == 1) {
+    plan = {true, kBN, kBN / 2, 1};
+  } else if (kind == 2) {
+    if ((bn != 128 && bn != 256) || split < 2 || split > kSplitMax || split > kblocks)
+      return B2_ERR_INVALID;
+    plan = {false, bn, bn, split};
+  } else if (kind >= 0) {
+    return B2_ERR_INVALID;
+  }
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, A, f, K, M, (uint64_t)K * es, kBM) ||
       !make_tmap(&tb, B, f, K, N, (uint64_t)K * es, plan.b_box_rows))
@@ -419,7 +485,7 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
   GemmArgs g{};
   g.M = M;
   g.N = N;
-  g.num_k_blocks = (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes);
+  g.num_k_blocks = kblocks;
   g.group_m = 16;
   g.out = C;
   g.ldo = ldc;
@@ -427,6 +493,31 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   if (f) return launch_dense<kEpiStore, true, float>(plan, ta, tb, g, di.sms, s);
   return launch_dense<kEpiStore, false, float>(plan, ta, tb, g, di.sms, s);
+}
+
+extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, int N, int K,
+                                int ldc, int dtype, int *status, b2_stream stream_) {
+  return gemm_nt_impl(A, B, C, M, N, K, ldc, dtype, -1, 0, 0, status, stream_);
+}
+
+extern "C" b2_status b2_gemm_nt_config(const void *A, const void *B, float *C, int M, int N,
+                                       int K, int ldc, int dtype, int kind, int bn, int split,
+                                       int *status, b2_stream stream_) {
+  if (kind < 0 || kind > 2) return B2_ERR_INVALID;
+  return gemm_nt_impl(A, B, C, M, N, K, ldc, dtype, kind, bn, split, status, stream_);
+}
+
+extern "C" b2_status b2_gemm_plan(int M, int N, int K, int dtype, int sms, int *kind, int *bn,
+                                  int *split) {
+  if (M <= 0 || N <= 0 || K <= 0 || sms <= 0 || !kind || !bn || !split ||
+      (dtype != B2_BF16 && dtype != B2_TF32))
+    return B2_ERR_INVALID;
+  const size_t es = dtype == B2_TF32 ? 4 : 2;
+  const DensePlan p = plan_dense(M, N, sms, false, (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes));
+  *kind = p.pair ? 1 : p.split > 1 ? 2 : 0;
+  *bn = p.bn;
+  *split = p.split;
+  return B2_OK;
 }
 
 extern "C" b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,

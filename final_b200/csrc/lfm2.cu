@@ -122,12 +122,13 @@ static b2_status dense_make(Arena &a, Stager &sg, DenseW *d, int K, const float 
 static b2_status dense_gemm(const CUtensorMap &ta, int M, const DenseW &W, float *C, long long ldc,
                             int *status, int sms, cudaStream_t s) {
   if (M <= 0) return B2_OK;
-  const DensePlan p = plan_dense(M, W.N, sms, false);
+  const int kblocks = (W.K * 2 + kBKBytes - 1) / kBKBytes;
+  const DensePlan p = plan_dense(M, W.N, sms, false, kblocks, splitk_cluster_caps(false));
   const CUtensorMap &tb = p.b_box_rows == 64 ? W.tm64 : p.b_box_rows == 128 ? W.tm128 : W.tm256;
   GemmArgs g{};
   g.M = M;
   g.N = W.N;
-  g.num_k_blocks = (W.K * 2 + kBKBytes - 1) / kBKBytes;
+  g.num_k_blocks = kblocks;
   g.out = C;
   g.ldo = ldc;
   g.status = status;

@@ -169,7 +169,7 @@ extern "C" b2_status b2_mlp_forward(b2_mlp *m, const float *x, float *y, int T,
   g1.out = m->inter;
   g1.ldo = Ip;
   g1.status = m->status;
-  const DensePlan p1 = plan_dense(T, Ip, m->sms, true);
+  const DensePlan p1 = plan_dense(T, Ip, m->sms, true, g1.num_k_blocks, splitk_cluster_caps(true));
   const CUtensorMap &tb1 = p1.b_box_rows == 128 ? m->tm_w13_128 : m->tm_w13_256;
   if (f)
     B2_RETURN_IF((launch_dense<kEpiSwiGLU, true, float>(p1, *ta, tb1, g1, m->sms, s)));
@@ -183,7 +183,7 @@ extern "C" b2_status b2_mlp_forward(b2_mlp *m, const float *x, float *y, int T,
   g2.out = y;
   g2.ldo = H;
   g2.status = m->status;
-  const DensePlan p2 = plan_dense(T, H, m->sms, false);
+  const DensePlan p2 = plan_dense(T, H, m->sms, false, g2.num_k_blocks, splitk_cluster_caps(false));
   const CUtensorMap &tb2 = p2.b_box_rows == 64    ? m->tm_w2_64
                            : p2.b_box_rows == 128 ? m->tm_w2_128
                                                   : m->tm_w2_256;

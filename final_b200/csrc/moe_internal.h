@@ -14,6 +14,7 @@
 #include "../../include/b2moe.h"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
+#include "gemm_sm100_splitk.cuh"
 #include "host_tmap.h"
 #include "moe_kernels.cuh"
 
@@ -135,26 +136,106 @@ b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const G
   return B2_OK;
 }
 
-// Kernel configuration of a dense (single-group) GEMM over M rows and
-// n_tiles 256-wide B tiles (for SwiGLU a 256-wide B tile gives 128 outputs).
-//   pair  CTA-pair kernel (256x256 tiles) when they keep every pair busy;
-//   bn    else the single-CTA kernel's tile width: the widest of 256 / 128 /
-//         64 that gives every SM a tile (SwiGLU always 256: its B tile holds
-//         128 gate and 128 up rows).
+// Kernel configuration of a dense (single-group) GEMM over M rows and N
+// output columns (for SwiGLU a 256-wide B tile gives 128 outputs), from
+// measured B200 behaviour (every configuration timed on the same shapes):
+//   pair   CTA-pair kernel (256x256 tiles) when they keep every pair busy;
+//   else small products are bound by how fast each SM pulls its operands
+//   from L2 (~70-100 GB/s per SM, ~9 TB/s in all) and by wave count, so:
+//   single 128-column tiles when they fit one wave;
+//   split  split-K over 128-column tiles (256 for SwiGLU) when those tiles
+//          fill at most half the SMs: `split` CTAs (a cluster) per tile, the
+//          most that still run as one wave of co-resident clusters
+//          (max_clusters[s] = co-resident clusters of size s, from the
+//          device; kSplitMax caps it), each with >= 4 k-blocks;
+//   bn     else the widest single-CTA tile that gives every SM a tile, or 64.
+// kb = 128-byte k-blocks of K (0: no split-K).
 struct DensePlan {
   bool pair;
   int bn;
   int b_box_rows;  // rows of the B tensor map's box
+  int split;       // CTAs per tile along K (1: no split)
 };
 
-inline DensePlan plan_dense(long long M, int N, int sms, bool swiglu) {
+constexpr int kSplitPlanMax = 6;  // clusters of 7-8 rarely all fit one wave on 148 SMs
+
+// Co-resident clusters of size s when the device was not asked: B200 GPCs
+// hold ~18 SMs each, and a cluster must sit inside one GPC.
+inline int static_max_clusters(int sms, int s) { return (sms / 18) * (18 / s); }
+
+inline DensePlan plan_dense(long long M, int N, int sms, bool swiglu, int kb = 0,
+                            const int *max_clusters = nullptr) {
   const long long nt256 = swiglu ? N / 128 : (N + kBN - 1) / kBN;
-  if (((M + kPairBM - 1) / kPairBM) * nt256 >= sms / 2) return {true, kBN, kBN / 2};
-  if (swiglu) return {false, kBN, kBN};
+  if (((M + kPairBM - 1) / kPairBM) * nt256 >= sms / 2) return {true, kBN, kBN / 2, 1};
   const long long mt = (M + kBM - 1) / kBM;
+  const int sbn = swiglu ? 256 : 128;  // split-K tile width
+  const long long tiles = mt * (swiglu ? N / 128 : (N + 127) / 128);
+  if (kb >= 8 && tiles * 2 <= sms) {
+    for (int sp = std::min<long long>(kSplitPlanMax, std::min<long long>(sms / tiles, kb / 4));
+         sp >= 2; --sp) {
+      const int cap = max_clusters ? max_clusters[sp] : static_max_clusters(sms, sp);
+      if (tiles <= cap) return {false, sbn, sbn, sp};
+    }
+  }
+  if (swiglu) return {false, kBN, kBN, 1};
+  if (tiles <= sms) return {false, 128, 128, 1};
   for (int c : {256, 128})
-    if (mt * ((N + c - 1) / c) >= sms) return {false, c, c};
-  return {false, 64, 64};
+    if (mt * ((N + c - 1) / c) >= sms) return {false, c, c, 1};
+  return {false, 64, 64, 1};
+}
+
+// Co-resident clusters of each size 2..kSplitMax for the split-K kernels on
+// the current device (cudaOccupancyMaxActiveClusters), queried once per
+// device; [bn == 256][size].  Falls back to the static estimate.
+const int *splitk_cluster_caps(bool swiglu_width);
+
+// The split-K kernel over one wave of clusters (plan.split CTAs per tile).
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_gemm_splitk(const DensePlan &plan, const CUtensorMap &ta, const CUtensorMap &tb,
+                             const GemmArgs &g, cudaStream_t s) {
+  SplitArgs a{};
+  a.M = g.M;
+  a.N = g.N;
+  a.num_k_blocks = g.num_k_blocks;
+  a.splits = plan.split;
+  a.m_tiles = (g.M + kBM - 1) / kBM;
+  a.out = g.out;
+  a.ldo = g.ldo;
+  a.status = g.status;
+  const int n_tiles = EPI == kEpiSwiGLU ? g.N / 128 : (g.N + plan.bn - 1) / plan.bn;
+  const int grid = a.m_tiles * n_tiles * plan.split;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = plan.split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (plan.bn == 256) {
+    auto kern = gemm_splitk_kernel<EPI, TF32, TOut, 256>;
+    static std::atomic<uint64_t> done{0};
+    B2_RETURN_IF(ensure_smem_limit(kern, splitk_smem_bytes(256), done));
+    cfg.dynamicSmemBytes = splitk_smem_bytes(256);
+    if (grid > 0) B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+  } else {
+    if constexpr (EPI == kEpiStore) {
+      auto kern = gemm_splitk_kernel<EPI, TF32, TOut, 128>;
+      static std::atomic<uint64_t> done{0};
+      B2_RETURN_IF(ensure_smem_limit(kern, splitk_smem_bytes(128), done));
+      cfg.dynamicSmemBytes = splitk_smem_bytes(128);
+      if (grid > 0) B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+    } else {
+      return B2_ERR_INVALID;
+    }
+  }
+  if (grid > 0) B2_LAUNCHED();
+  return B2_OK;
 }
 
 // Launches a dense GEMM planned by plan_dense.  g.M, g.N, g.num_k_blocks,
@@ -175,6 +256,7 @@ b2_status launch_dense(const DensePlan &plan, const CUtensorMap &ta, const CUten
     const int pairs = (int)std::min<long long>(sms / 2, mt_pair * g.num_n_tiles);
     return launch_gemm_pair<EPI, TF32, TOut>(ta, tb, g, pairs, s);
   }
+  if (plan.split > 1) return launch_gemm_splitk<EPI, TF32, TOut>(plan, ta, tb, g, s);
   const int grid = (int)std::min<long long>(sms, mt * g.num_n_tiles);
   if constexpr (EPI == kEpiSwiGLU) {
     return launch_gemm<EPI, TF32, TOut, 256>(ta, tb, g, grid, s);

@@ -144,12 +144,17 @@ class SparseMoeBlock:
             pass
 
 
+_KINDS = {"single": 0, "pair": 1, "splitk": 2}
+
+
 def gemm_nt(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
             dtype: str = "bf16", status: Optional[torch.Tensor] = None,
-            stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+            stream: Optional[torch.cuda.Stream] = None, config=None) -> torch.Tensor:
     """C[M,N] fp32 = A[M,K] . B[N,K]^T on the tcgen05 core.
 
     dtype "bf16": A, B bf16.  dtype "tf32": A, B fp32 (TF32 tensor-core math).
+    config: None (the planner's choice) or (kind, bn, split) as gemm_plan
+    returns it, to run one kernel configuration (b2_gemm_nt_config).
     Replaces attn_matmul_tiled_kernel (src/layer.cu:9-141) and the LM-head
     GEMM (src/model.cu:42-116).
     """
@@ -161,9 +166,14 @@ def gemm_nt(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None
     if out is None:
         out = torch.empty(M, N, dtype=torch.float32, device=A.device)
     st = C.c_void_p(status.data_ptr()) if status is not None else None
-    check(lib.b2_gemm_nt(C.c_void_p(A.data_ptr()), C.c_void_p(B.data_ptr()),
-                         C.c_void_p(out.data_ptr()), M, N, K, out.stride(0), _DT[dtype], st,
-                         C.c_void_p(_stream_ptr(stream))), "b2_gemm_nt")
+    args = (C.c_void_p(A.data_ptr()), C.c_void_p(B.data_ptr()), C.c_void_p(out.data_ptr()), M,
+            N, K, out.stride(0), _DT[dtype])
+    if config is None:
+        check(lib.b2_gemm_nt(*args, st, C.c_void_p(_stream_ptr(stream))), "b2_gemm_nt")
+    else:
+        kind, bn, split = config
+        check(lib.b2_gemm_nt_config(*args, _KINDS[kind], bn, split, st,
+                                    C.c_void_p(_stream_ptr(stream))), "b2_gemm_nt_config")
     return out
 
 
@@ -180,3 +190,13 @@ def to_bf16(x: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> torc
 
 def launch_count() -> int:
     return int(_lib.load().b2_kernel_launch_count())
+
+
+def gemm_plan(M: int, N: int, K: int, dtype: str = "bf16", sms: int = 148):
+    """The kernel b2_gemm_nt picks for an M x N x K product on `sms` SMs:
+    ("single" | "pair" | "splitk", tile width, K splits).  Host only."""
+    lib = _lib.load()
+    kind, bn, split = C.c_int(), C.c_int(), C.c_int()
+    check(lib.b2_gemm_plan(M, N, K, _DT[dtype], sms, C.byref(kind), C.byref(bn), C.byref(split)),
+          "b2_gemm_plan")
+    return ("single", "pair", "splitk")[kind.value], bn.value, split.value

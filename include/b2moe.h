@@ -151,6 +151,24 @@ size_t b2_moe_device_bytes(const b2_moe *moe);
 b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, int N,
                      int K, int ldc, int dtype, int *status, b2_stream stream);
 
+/* b2_gemm_nt with the kernel configuration chosen by the caller instead of
+ * the planner (tuning sweeps, tests that reach every kernel on one shape):
+ * kind 0 single-CTA tiles of width bn (64, 128, 256); 1 CTA pairs
+ * (256 x 256); 2 split-K clusters of `split` CTAs (2..8) over 128 x bn tiles
+ * (bn 128 or 256).  No counterpart in the reference. */
+b2_status b2_gemm_nt_config(const void *A, const void *B, float *C, int M, int N,
+                            int K, int ldc, int dtype, int kind, int bn, int split,
+                            int *status, b2_stream stream);
+
+/* The kernel configuration b2_gemm_nt uses for an M x N x K product on a
+ * device with `sms` SMs (host only, no device call): *kind = 0 single-CTA
+ * tiles, 1 CTA pairs (256 x 256), 2 split-K clusters; *bn = output tile
+ * width; *split = CTAs per tile along K (1 unless kind == 2).  No
+ * counterpart in the reference, whose GEMM has one fixed 128 x 128 tiling
+ * (src/layer.cu:9-141). */
+b2_status b2_gemm_plan(int M, int N, int K, int dtype, int sms, int *kind, int *bn,
+                       int *split);
+
 /* fp32 -> bf16 (round to nearest even), n elements, device pointers. */
 b2_status b2_convert_f32_to_bf16(const float *in, void *out, size_t n,
                                  b2_stream stream);

@@ -15,21 +15,30 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-# On 148 SMs the shapes below reach every kernel configuration: CTA pairs
-# (256x256 tiles) and single CTAs with 256-, 128- and 64-column tiles.
+# Shapes across the planner's choices on 148 SMs (final_b200.moe.gemm_plan):
+# CTA pairs (256x256 tiles), single CTAs with 128-column tiles, split-K
+# clusters of 2..6 CTAs; test_every_configuration below runs every kernel
+# configuration, chosen or not, on the same operands.
 SHAPES = [
-    (128, 256, 64),
-    (200, 300, 128),      # ragged M and N, one partial k-block (64-column tiles)
-    (512, 2048, 2048),    # out projection, M=512 (64-column tiles)
-    (1280, 2048, 2048),   # 128-column tiles
-    (300, 1000, 512),     # 64-column tiles, ragged last column tile
+    (128, 256, 64),       # one k-block
+    (200, 300, 128),      # ragged M and N, partial k-blocks
+    (512, 2048, 2048),    # out projection, M=512: split-K 2 x 128
+    (1280, 2048, 2048),   # single CTA, 128-column tiles, two waves
+    (300, 1000, 512),     # ragged split-K 2 x 128
     (384, 3072, 2048),    # fused QKV width
-    (64, 65536, 2048),    # LM head, batch rows only
-    (1, 512, 2048),       # single row
-    (1000, 520, 1032),    # K not a multiple of the 64-wide k-block
+    (64, 65536, 2048),    # LM head, batch rows only (CTA pairs)
+    (1, 512, 2048),       # single row: split-K 6
+    (1000, 520, 1032),    # K not a multiple of the 64-wide k-block: split-K 3
     (4096, 3072, 2048),   # enough 256x256 tiles for the CTA-pair kernel
     (2000, 4096, 1024),   # CTA-pair kernel with a ragged last row tile
+    (512, 3072, 2048),    # single CTA, 128-column tiles, one wave
+    (64, 2048, 7168),     # decode-size down projection: split-K 6
+    (1, 4096, 2048),      # one token: split-K 4
+    (333, 1000, 1000),    # ragged split-K 4
 ]
+
+CONFIGS = ([("single", bn, 1) for bn in (64, 128, 256)] + [("pair", 256, 1)] +
+           [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)])
 
 
 def _rel(a, b):
@@ -50,7 +59,7 @@ def test_gemm_bf16_vs_fp64(cuda_dev, M, N, K):
     assert _rel(Cm, ref) < 1e-4
 
 
-@pytest.mark.parametrize("M,N,K", SHAPES[:5])
+@pytest.mark.parametrize("M,N,K", SHAPES[:5] + [(1000, 520, 1032), (64, 2048, 7168)])
 def test_gemm_tf32_vs_fp64(cuda_dev, M, N, K):
     from final_b200 import gemm_nt
     g = torch.Generator(device=cuda_dev).manual_seed(M + N + K)
@@ -107,3 +116,35 @@ def test_gemm_invalid_args(cuda_dev):
     B = torch.zeros(8, 12, device=cuda_dev, dtype=torch.bfloat16)
     with pytest.raises(B2Error):
         gemm_nt(A, B, dtype="bf16")
+
+
+@pytest.mark.parametrize("M,N,K", [(333, 1000, 1000), (512, 2048, 2048), (64, 520, 7168)])
+@pytest.mark.parametrize("dtype", ["bf16", "tf32"])
+def test_every_configuration(cuda_dev, M, N, K, dtype):
+    """Every kernel configuration (b2_gemm_nt_config) on the same operands:
+    single-CTA 64/128/256-column tiles, CTA pairs, split-K with 128/256-column
+    tiles and 2..8 CTAs per cluster."""
+    from final_b200 import gemm_nt
+    g = torch.Generator(device=cuda_dev).manual_seed(M + 3 * N + 7 * K)
+    A = torch.randn(M, K, device=cuda_dev, generator=g)
+    B = torch.randn(N, K, device=cuda_dev, generator=g) * 0.02
+    if dtype == "bf16":
+        A, B = A.to(torch.bfloat16), B.to(torch.bfloat16)
+    ref = A.double() @ B.double().T
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    for cfg in CONFIGS:
+        Cm = gemm_nt(A, B, dtype=dtype, status=status, config=cfg)
+        torch.cuda.synchronize()
+        assert status.item() == 0, cfg
+        assert _rel(Cm, ref) < (1e-4 if dtype == "bf16" else 1e-2), cfg
+
+
+def test_splitk_is_deterministic(cuda_dev):
+    """The split-K reduction runs in a fixed CTA order: repeated calls give
+    identical bits."""
+    from final_b200 import gemm_nt
+    A = torch.randn(512, 2048, device=cuda_dev).to(torch.bfloat16)
+    B = (torch.randn(3072, 2048, device=cuda_dev) * 0.02).to(torch.bfloat16)
+    c0 = gemm_nt(A, B, dtype="bf16")
+    for _ in range(3):
+        assert torch.equal(gemm_nt(A, B, dtype="bf16"), c0)
