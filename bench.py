@@ -431,10 +431,12 @@ def run_ours(args, rank, world, dev):
     if not args.no_dense and rank == 0:
         out["dense_gemm_sweep"] = dense_sweep(dev)
         out["dense_mlp"] = mlp_bench(dev)
-    if not args.no_model and rank == 0 and world == 1:
+    if not args.no_model:
         del layer
         torch.cuda.empty_cache()
-        out["full_model"] = model_bench(dev)
+        fm = model_bench(dev, rank=rank, world=world)
+        if rank == 0:
+            out["full_model"] = fm
     if w_host is not None:
         out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
     return out
@@ -602,20 +604,24 @@ def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
 
 
 # ------------------------------------------------------------------ model
-def model_bench(dev, B=32, S=512, steps=5, warmup=3):
+def model_bench(dev, B=32, S=512, steps=5, warmup=3, rank=0, world=1):
     """Config 5: the whole LFM2-8B-A1B-shaped model (24 layers, random-init
     weights, vocab 65536) over batch 32 x seq 512 token ids uniform in
     [0, 65536): samples/s of the last-token logits, device-timed with inputs
     resident, and end to end with the ids copied from pinned host memory and
-    the logits copied back every step."""
+    the logits copied back every step.  With several ranks every GPU holds a
+    replica of the model (36 GB of its 180 GB) and runs its own batch of 32:
+    no activation crosses NVLink; samples/s counts all ranks' samples over the
+    slowest rank's time (barrier before and after, max over ranks)."""
     import torch
+    import torch.distributed as dist
     from final_b200 import launch_count
     from final_b200.lfm2 import LFM2Model, model_flop, synthetic_weights
     t0 = time.time()
     model = LFM2Model(synthetic_weights(dev, seed=11), max_batch=B, max_seq=S, device=dev)
     torch.cuda.empty_cache()
     build_s = time.time() - t0
-    g = torch.Generator(device=dev).manual_seed(12)
+    g = torch.Generator(device=dev).manual_seed(12 + 1000 * rank)
     ids = torch.randint(0, 65536, (B, S), device=dev, generator=g, dtype=torch.int32)
     logits = torch.empty(B, 65536, device=dev)
     stream = torch.cuda.current_stream()
@@ -625,8 +631,19 @@ def model_bench(dev, B=32, S=512, steps=5, warmup=3):
     st = model.device_status()
     if st:
         raise RuntimeError(f"model device status 0x{st:x}")
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
     sampler = ClockSampler(smi_index_for(dev.index))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     sampler.start()
     n0 = launch_count()
     e0.record(stream)
@@ -636,11 +653,13 @@ def model_bench(dev, B=32, S=512, steps=5, warmup=3):
     torch.cuda.synchronize()
     n1 = launch_count()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
     # end to end: ids from pinned host memory, logits back to pinned host memory
     ids_h = ids.cpu().pin_memory()
     logits_h = torch.empty(B, 65536, dtype=torch.float32).pin_memory()
     ids_d = torch.empty_like(ids)
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(steps):
@@ -649,19 +668,21 @@ def model_bench(dev, B=32, S=512, steps=5, warmup=3):
         logits_h.copy_(logits, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
-    ems = e0.elapsed_time(e1) / steps
+    ems = max_over_ranks(e0.elapsed_time(e1) / steps)
     st = model.device_status()
     if st:
         raise RuntimeError(f"model device status 0x{st:x}")
     flop = model_flop(B, S)
     pk = peaks()
-    out = {"workload": "lfm2_8b_a1b_shaped_forward", "batch": B, "seq_len": S, "layers": 24,
-           "vocab": 65536, "weights": "random init (bf16 projections / experts from fp32)",
-           "samples_per_s": B / (ms / 1e3), "tokens_per_s": B * S / (ms / 1e3),
-           "ms_per_forward": ms, "tflops": flop / (ms / 1e3) / 1e12,
+    out = {"workload": "lfm2_8b_a1b_shaped_forward", "batch_per_gpu": B, "seq_len": S,
+           "layers": 24, "vocab": 65536, "n_gpus": world,
+           "parallelism": "single" if world == 1 else f"replica per GPU x{world}",
+           "scaling": "weak", "weights": "random init (bf16 projections / experts from fp32)",
+           "samples_per_s": B * world / (ms / 1e3), "tokens_per_s": B * S * world / (ms / 1e3),
+           "ms_per_forward": ms, "tflops_per_gpu": flop / (ms / 1e3) / 1e12,
            "frac_of_bf16_peak": flop / (ms / 1e3) / 1e12 / pk["bf16"],
            "flop_per_forward": flop, "gpu_launches_per_forward": int(n1 - n0) // steps,
-           "e2e": {"samples_per_s": B / (ems / 1e3), "ms_per_step": ems,
+           "e2e": {"samples_per_s": B * world / (ems / 1e3), "ms_per_step": ems,
                    "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": B * 65536 * 4},
            "device_bytes": model.device_bytes(), "build_s": build_s, "clocks": clocks,
            "steps": steps, "warmup": warmup}
@@ -816,7 +837,11 @@ def main():
         print(json.dumps(gemm_configs(args, dev)), flush=True)
         return 0
     if args.model_only:
-        print(json.dumps(model_bench(dev, steps=args.steps, warmup=args.warmup)), flush=True)
+        fm = model_bench(dev, steps=args.steps, warmup=args.warmup, rank=rank, world=world)
+        if rank == 0:
+            print(json.dumps(fm), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return 0
     try:
         out = run_ours(args, rank, world, dev)
