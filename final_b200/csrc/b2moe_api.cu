@@ -340,17 +340,18 @@ b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap 
   return B2_OK;
 }
 
-b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s) {
+b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s, bool accumulate) {
   const int K = m->d.top_k, H = m->d.hidden;
+  const int acc = accumulate ? 1 : 0;
   prof_mark(m, s);
   if (m->tf32)
     B2_RETURN_IF(launch_pdl(combine_kernel<float>, dim3(T), dim3(256), 0, s,
                             reinterpret_cast<const float *>(m->sout), (const int *)m->token_slot,
-                            (const float *)m->topk_w, T, H, K, y));
+                            (const float *)m->topk_w, T, H, K, y, acc));
   else
     B2_RETURN_IF(launch_pdl(combine_kernel<__nv_bfloat16>, dim3(T), dim3(256), 0, s,
                             reinterpret_cast<const __nv_bfloat16 *>(m->sout),
-                            (const int *)m->token_slot, (const float *)m->topk_w, T, H, K, y));
+                            (const int *)m->token_slot, (const float *)m->topk_w, T, H, K, y, acc));
   prof_mark(m, s);
   return B2_OK;
 }
@@ -375,11 +376,15 @@ static b2_status copy_trace(void *dst, const void *src, size_t bytes, cudaStream
 
 extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int T,
                                        const b2_moe_trace *tr, b2_stream stream_) {
+  return moe_forward_impl(m, x, y, T, tr, reinterpret_cast<cudaStream_t>(stream_), false);
+}
+
+b2_status b2::moe_forward_impl(b2_moe *m, const float *x, float *y, int T,
+                               const b2_moe_trace *tr, cudaStream_t s, bool accumulate) {
   if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
   if (m->n_wexp != m->d.num_experts || !m->inter) return B2_ERR_INVALID;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   if (T == 0) return B2_OK;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   const int E = m->d.num_experts, K = m->d.top_k;
 
   B2_RETURN_IF(moe_route_stage(m, x, T, tr, s));
@@ -391,7 +396,7 @@ extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int 
   sc.num_groups = E;
   sc.mtiles_upper_bound = ((long long)T * K + kPairBM - 1) / kPairBM + E;  // <= 1 partial tile per expert
   B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, m->tm_inter, m->inter, m->sout, sc, s));
-  B2_RETURN_IF(moe_combine_stage(m, y, T, s));
+  B2_RETURN_IF(moe_combine_stage(m, y, T, s, accumulate));
 
   if (tr) {
     const size_t tk = (size_t)T * K;

@@ -62,6 +62,7 @@ struct GemmArgs {
   void *out;
   long long ldo;             // output row stride in elements
   int *status;
+  int accumulate;            // fp32 output only: C += A . B^T (the residual add, fused)
 };
 
 // Ring depth for an N-tile width: 192 KB of A+B stages (4 at 256, 6 at 128,
@@ -129,8 +130,13 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int *s
 // Store up to 32 consecutive fp32 values of one output row as TOut.
 template <typename TOut>
 __device__ __forceinline__ void store_cols(TOut *dst, const float (&h)[32], int valid,
-                                           bool vec_ok) {
+                                           bool vec_ok, bool add = false) {
   if (valid <= 0) return;
+  if (add) {  // fp32 accumulate into C: C = C + result, element by element
+    if constexpr (sizeof(TOut) == 4)
+      for (int i = 0; i < 32 && i < valid; ++i) dst[i] = __fadd_rn(dst[i], h[i]);
+    return;
+  }
   if (valid >= 32 && vec_ok) {
     if constexpr (sizeof(TOut) == 2) {
       uint4 *d = reinterpret_cast<uint4 *>(dst);
@@ -165,7 +171,7 @@ __device__ __forceinline__ void store_cols(TOut *dst, const float (&h)[32], int 
 template <typename TOut>
 __device__ __forceinline__ void store_block_coalesced(uint8_t *stage, const float (&h)[32],
                                                       TOut *out0, long long ldo, int rows_valid,
-                                                      int lane) {
+                                                      int lane, bool add = false) {
   if constexpr (sizeof(TOut) == 4) {
     float4 *srow = reinterpret_cast<float4 *>(stage + lane * 128);
 #pragma unroll
@@ -173,11 +179,31 @@ __device__ __forceinline__ void store_block_coalesced(uint8_t *stage, const floa
       srow[u ^ (lane & 7)] = make_float4(h[4 * u], h[4 * u + 1], h[4 * u + 2], h[4 * u + 3]);
     __syncwarp();
     const int u = lane & 7;
+    if (add) {
+      // C = C + result: all eight loads of C are in flight before any store
+      float4 o[8];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int r = it * 4 + (lane >> 3);
-      const float4 v = reinterpret_cast<const float4 *>(stage + r * 128)[u ^ (r & 7)];
-      if (r < rows_valid) reinterpret_cast<float4 *>(out0 + r * ldo)[u] = v;
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        o[it] = r < rows_valid ? reinterpret_cast<const float4 *>(out0 + r * ldo)[u]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        const float4 v = reinterpret_cast<const float4 *>(stage + r * 128)[u ^ (r & 7)];
+        if (r < rows_valid)
+          reinterpret_cast<float4 *>(out0 + r * ldo)[u] =
+              make_float4(__fadd_rn(o[it].x, v.x), __fadd_rn(o[it].y, v.y),
+                          __fadd_rn(o[it].z, v.z), __fadd_rn(o[it].w, v.w));
+      }
+    } else {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        const float4 v = reinterpret_cast<const float4 *>(stage + r * 128)[u ^ (r & 7)];
+        if (r < rows_valid) reinterpret_cast<float4 *>(out0 + r * ldo)[u] = v;
+      }
     }
   } else {
     uint4 *srow = reinterpret_cast<uint4 *>(stage + lane * 64);
@@ -204,12 +230,12 @@ __device__ __forceinline__ void store_block_coalesced(uint8_t *stage, const floa
 template <typename TOut>
 __device__ __forceinline__ void store_chunk(uint8_t *stage, const float (&h)[32], TOut *out0,
                                            long long ldo, int rows_valid, int cols_valid,
-                                           bool vec_ok, int lane) {
+                                           bool vec_ok, int lane, bool add = false) {
   if (rows_valid <= 0 || cols_valid <= 0) return;
   if (vec_ok && cols_valid >= 32) {
-    store_block_coalesced(stage, h, out0, ldo, rows_valid, lane);
+    store_block_coalesced(stage, h, out0, ldo, rows_valid, lane, add);
   } else if (lane < rows_valid) {
-    store_cols(out0 + lane * ldo, h, cols_valid, vec_ok);
+    store_cols(out0 + lane * ldo, h, cols_valid, vec_ok, add);
   }
 }
 
@@ -416,7 +442,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) h[i] = __uint_as_float(r[i]);
           store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
-                      lane);
+                      lane, g.accumulate != 0);
         }
       }
       tc_fence_before();

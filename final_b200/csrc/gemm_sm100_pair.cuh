@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) h[i] = __uint_as_float(r[i]);
           store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
-                      lane);
+                      lane, g.accumulate != 0);
         }
       }
       tc_fence_before();

@@ -48,6 +48,7 @@ struct SplitArgs {
   void *out;
   long long ldo;         // output row stride (elements)
   int *status;
+  int accumulate;        // fp32 plain epilogue only: C += result
 };
 
 constexpr int splitk_stages(int bn) { return bn == 256 ? 3 : 4; }
@@ -76,7 +77,14 @@ __device__ __forceinline__ uint32_t part_off(int row, int u) {
 // store when aligned and whole, else element by element up to n_valid).
 template <typename TOut>
 __device__ __forceinline__ void store4(TOut *dst, float a, float b, float c, float d, bool vec,
-                                       int n_valid) {
+                                       int n_valid, bool add = false) {
+  if constexpr (sizeof(TOut) == 4) {
+    if (add) {  // C = C + result
+      const float v[4] = {a, b, c, d};
+      for (int i = 0; i < 4 && i < n_valid; ++i) dst[i] = __fadd_rn(dst[i], v[i]);
+      return;
+    }
+  }
   if (vec && n_valid >= 4) {
     if constexpr (sizeof(TOut) == 4)
       *reinterpret_cast<float4 *>(dst) = make_float4(a, b, c, d);
@@ -282,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 acc.w += v[w][j].w;
               }
             store4(out + (long long)grow * g.ldo + gcol, acc.x, acc.y, acc.z, acc.w, vec_ok,
-                   g.N - gcol);
+                   g.N - gcol, g.accumulate != 0);
           }
         }
       } else {

@@ -5,10 +5,10 @@
 // Every projection is one call of the dense tcgen05 GEMM (gemm_sm100*.cuh)
 // with bf16 operands and fp32 output; the glue between them is the
 // kernels of lfm2_kernels.cuh.  A decoder layer is
-//   add_rmsnorm(resid += ffn_out_prev) -> xb bf16
-//   attention:  xb.Wqkv^T -> qk_norm_rope -> flash_attn -> core.Wo^T -> mix
-//   short conv: xb.Win^T  -> conv_glue                  -> core.Wout^T -> mix
-//   add_rmsnorm(resid += mix) -> hn fp32 -> MoE (b2_moe) or MLP (b2_mlp)
+//   rmsnorm(resid) -> xb bf16
+//   attention:  xb.Wqkv^T -> qk_norm_rope -> flash_attn -> resid += core.Wo^T
+//   short conv: xb.Win^T  -> conv_glue                  -> resid += core.Wout^T
+//   rmsnorm(resid) -> hn fp32 -> MoE (b2_moe) or MLP (b2_mlp), adding into resid
 // with every launch programmatic-dependent on its predecessor.  The layers
 // of a model share one workspace (the activations between the projections);
 // each layer owns only its packed weights.
@@ -117,10 +117,11 @@ static b2_status dense_make(Arena &a, Stager &sg, DenseW *d, int K, const float 
   return dense_maps(d) ? B2_OK : B2_ERR_CUDA;
 }
 
-// C[M][N] (fp32, row stride ldc) = A . W^T; ta is a bf16 map over A's rows
-// with 128-row boxes and K inner elements.
-static b2_status dense_gemm(const CUtensorMap &ta, int M, const DenseW &W, float *C, long long ldc,
-                            int *status, int sms, cudaStream_t s) {
+// C[M][N] (fp32 or bf16, row stride ldc) = A . W^T; ta is a bf16 map over
+// A's rows with 128-row boxes and K inner elements.
+template <typename TOut>
+static b2_status dense_gemm(const CUtensorMap &ta, int M, const DenseW &W, TOut *C, long long ldc,
+                            int *status, int sms, cudaStream_t s, bool accumulate = false) {
   if (M <= 0) return B2_OK;
   const int kblocks = (W.K * 2 + kBKBytes - 1) / kBKBytes;
   const DensePlan p = plan_dense(M, W.N, sms, false, kblocks, splitk_cluster_caps(false));
@@ -132,13 +133,14 @@ static b2_status dense_gemm(const CUtensorMap &ta, int M, const DenseW &W, float
   g.out = C;
   g.ldo = ldc;
   g.status = status;
-  return launch_dense<kEpiStore, false, float>(p, ta, tb, g, sms, s);
+  g.accumulate = accumulate ? 1 : 0;
+  return launch_dense<kEpiStore, false, TOut>(p, ta, tb, g, sms, s);
 }
 
 // Activations between the projections, shared by every layer of a model.
 struct Work {
   int maxT = 0, H = 0, Hq = 0, Hkv = 0;
-  float *wide = nullptr;             // [maxT][max((Hq+2Hkv)*64, 3H)] fp32 projection output
+  __nv_bfloat16 *wide = nullptr;     // [maxT][max((Hq+2Hkv)*64, 3H)] bf16 projection output
   __nv_bfloat16 *q = nullptr;        // [maxT * Hq * 64]  ([B][Hq][S][64])
   __nv_bfloat16 *k = nullptr, *v = nullptr;  // [maxT * Hkv * 64]
   __nv_bfloat16 *xb = nullptr;       // [maxT][H] normed input (A of the first projection)
@@ -211,31 +213,33 @@ static b2_status conv_make(Arena &a, Stager &sg, ConvW *w, int H, const float *c
   return sg.copy(conv_w, w->cw, (size_t)H * kConvL);
 }
 
-// y[T][H] = attention block of w.xb (already normed, bf16).
+// y[T][H] = attention block of w.xb (already normed, bf16); accumulate: y +=.
 static b2_status attn_run(const AttnW &a, const Work &w, int B, int S, const float *cos,
-                          const float *sin, float *y, int *status, int sms, cudaStream_t s) {
+                          const float *sin, float *y, int *status, int sms, cudaStream_t s,
+                          bool accumulate = false) {
   const int T = B * S;
   const int W3 = a.qkv.N;
   B2_RETURN_IF(dense_gemm(w.tm_xb, T, a.qkv, w.wide, W3, status, sms, s));
-  B2_RETURN_IF(launch_pdl(qk_norm_rope_kernel, dim3(T), dim3(256), 0, s, (const float *)w.wide,
+  B2_RETURN_IF(launch_pdl(qk_norm_rope_kernel, dim3(T), dim3(256), 0, s,
+                          (const __nv_bfloat16 *)w.wide,
                           (const float *)a.q_ln, (const float *)a.k_ln, cos, sin, S, a.Hq, a.Hkv,
                           a.eps, w.q, w.k, w.v));
   const float scale_log2 = (1.0f / sqrtf(64.0f)) * 1.4426950408889634f;
   B2_RETURN_IF(launch_pdl(flash_attn_kernel, dim3((S + kAttnB - 1) / kAttnB, a.Hq, B), dim3(128),
                           0, s, (const __nv_bfloat16 *)w.q, (const __nv_bfloat16 *)w.k,
                           (const __nv_bfloat16 *)w.v, S, a.Hq, a.Hkv, scale_log2, w.core));
-  return dense_gemm(w.tm_core_attn, T, a.o, y, a.H, status, sms, s);
+  return dense_gemm(w.tm_core_attn, T, a.o, y, a.H, status, sms, s, accumulate);
 }
 
-// y[T][H] = short-conv block of w.xb.
+// y[T][H] = short-conv block of w.xb; accumulate: y +=.
 static b2_status conv_run(const ConvW &c, const Work &w, int B, int S, float *y, int *status,
-                          int sms, cudaStream_t s) {
+                          int sms, cudaStream_t s, bool accumulate = false) {
   const int T = B * S, H = c.H;
   B2_RETURN_IF(dense_gemm(w.tm_xb, T, c.in, w.wide, 3LL * H, status, sms, s));
   B2_RETURN_IF(launch_pdl(conv_glue_kernel, dim3((H + 511) / 512, (S + kConvRun - 1) / kConvRun, B),
-                          dim3(128), 0, s, (const float *)w.wide, (const float *)c.cw, S, H,
-                          w.core));
-  return dense_gemm(w.tm_core_conv, T, c.out, y, H, status, sms, s);
+                          dim3(128), 0, s, (const __nv_bfloat16 *)w.wide, (const float *)c.cw, S,
+                          H, w.core));
+  return dense_gemm(w.tm_core_conv, T, c.out, y, H, status, sms, s, accumulate);
 }
 
 static b2_status to_bf16_async(const float *x, __nv_bfloat16 *out, size_t n, int sms,
@@ -463,7 +467,7 @@ struct b2_lfm2 {
   DenseW lm_head;               // [V][H] bf16
   float *final_norm = nullptr;  // [H]
   float *cos = nullptr, *sin = nullptr;  // [max_seq][64]
-  float *resid = nullptr, *delta = nullptr, *hn = nullptr;  // [maxT][H] fp32
+  float *resid = nullptr, *hn = nullptr;  // [maxT][H] fp32: residual stream, FFN input
   __nv_bfloat16 *lastb = nullptr;  // [max_batch][H]
   CUtensorMap tm_lastb;
   int *status = nullptr;
@@ -544,7 +548,6 @@ extern "C" b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, 
   B2_TRY(cudaMemsetAsync(m->status, 0, sizeof(int), s) == cudaSuccess ? B2_OK : B2_ERR_CUDA);
   B2_TRY(work_make(m->mem, &m->work, (int)maxT, H, Hq, Hkv));
   B2_TRY(m->mem.get(&m->resid, maxT * H));
-  B2_TRY(m->mem.get(&m->delta, maxT * H));
   B2_TRY(m->mem.get(&m->hn, maxT * H));
   B2_TRY(m->mem.get(&m->lastb, (size_t)d.max_batch * H));
   B2_TRY(cudaMemsetAsync(m->lastb, 0, (size_t)d.max_batch * H * 2, s) == cudaSuccess ? B2_OK
@@ -648,38 +651,34 @@ static b2_status lfm2_forward_impl(b2_lfm2 *m, const int32_t *ids, int B, int S,
   const float eps = d.eps > 0 ? d.eps : 1e-5f;
   B2_RETURN_IF(launch_pdl(embed_kernel, dim3(T), dim3(256), 0, s, (const int *)ids,
                           (const float *)m->embed, H, d.vocab, m->resid, m->status));
+  // Every block adds its output into the residual stream inside its last
+  // kernel (the out projection's epilogue, the MoE combine, the MLP's down
+  // projection): DecoderLayer's two add_kernel passes (src/layer.cu:1905-1918)
+  // cost no separate read / write of the stream.
   for (int i = 0; i < d.num_layers; ++i) {
     Layer &L = m->layers[i];
-    // resid += previous FFN output; xb = operator_norm(resid)
-    B2_RETURN_IF(norm_launch(m->resid, i ? m->delta : nullptr, L.op_norm, T, H, 1, 0, 1, eps,
-                             nullptr, m->work.xb, s));
-    if (hidden_out && i > 0)
-      B2_CUDA(cudaMemcpyAsync(hidden_out + (size_t)(i - 1) * T * H, m->resid, (size_t)T * H * 4,
-                              cudaMemcpyDeviceToDevice, s));
+    // xb = operator_norm(resid)
+    B2_RETURN_IF(norm_launch(m->resid, nullptr, L.op_norm, T, H, 1, 0, 0, eps, nullptr,
+                             m->work.xb, s));
+    // resid += attention / short conv
     if (L.attention)
-      B2_RETURN_IF(attn_run(L.a, m->work, B, S, m->cos, m->sin, m->delta, m->status, m->sms, s));
+      B2_RETURN_IF(attn_run(L.a, m->work, B, S, m->cos, m->sin, m->resid, m->status, m->sms, s,
+                            true));
     else
-      B2_RETURN_IF(conv_run(L.c, m->work, B, S, m->delta, m->status, m->sms, s));
-    // resid += mixer output; hn = ffn_norm(resid)
-    B2_RETURN_IF(norm_launch(m->resid, m->delta, L.ffn_norm, T, H, 1, 0, 1, eps, m->hn, nullptr, s));
+      B2_RETURN_IF(conv_run(L.c, m->work, B, S, m->resid, m->status, m->sms, s, true));
+    // hn = ffn_norm(resid); resid += MoE / MLP
+    B2_RETURN_IF(norm_launch(m->resid, nullptr, L.ffn_norm, T, H, 1, 0, 0, eps, m->hn, nullptr, s));
     if (L.moe)
-      B2_RETURN_IF(b2_moe_forward(L.moe, m->hn, m->delta, T, reinterpret_cast<b2_stream>(s)));
+      B2_RETURN_IF(moe_forward_impl(L.moe, m->hn, m->resid, T, nullptr, s, true));
     else
-      B2_RETURN_IF(b2_mlp_forward(L.mlp, m->hn, m->delta, T, reinterpret_cast<b2_stream>(s)));
+      B2_RETURN_IF(mlp_forward_impl(L.mlp, m->hn, m->resid, T, s, true));
+    if (hidden_out)
+      B2_CUDA(cudaMemcpyAsync(hidden_out + (size_t)i * T * H, m->resid, (size_t)T * H * 4,
+                              cudaMemcpyDeviceToDevice, s));
   }
-  if (hidden_out) {
-    // the last layer's residual is otherwise only formed for the last tokens
-    B2_RETURN_IF(norm_launch(m->resid, m->delta, m->final_norm, T, H, 1, 0, 1, eps, nullptr,
-                             nullptr, s));
-    B2_CUDA(cudaMemcpyAsync(hidden_out + (size_t)(d.num_layers - 1) * T * H, m->resid,
-                            (size_t)T * H * 4, cudaMemcpyDeviceToDevice, s));
-    B2_RETURN_IF(norm_launch(m->resid, nullptr, m->final_norm, B, H, S, S - 1, 0, eps, nullptr,
-                             m->lastb, s));
-  } else {
-    // final norm of each sequence's last token only, with the last residual add fused
-    B2_RETURN_IF(norm_launch(m->resid, m->delta, m->final_norm, B, H, S, S - 1, 0, eps, nullptr,
-                             m->lastb, s));
-  }
+  // final norm of each sequence's last token only
+  B2_RETURN_IF(norm_launch(m->resid, nullptr, m->final_norm, B, H, S, S - 1, 0, eps, nullptr,
+                           m->lastb, s));
   return dense_gemm(m->tm_lastb, B, m->lm_head, logits, d.vocab, m->status, m->sms, s);
 }
 

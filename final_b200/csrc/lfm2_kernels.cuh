@@ -98,7 +98,8 @@ static __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------ q/k norm + RoPE
-// qkv: [T][(Hq + 2 Hkv) * 64] fp32 projections (q heads, k heads, v heads).
+// qkv: [T][(Hq + 2 Hkv) * 64] bf16 projections (q heads, k heads, v heads;
+// the projection GEMM writes bf16, half the bytes of fp32 both ways).
 // One block per token, one warp per head (lane l holds elements l and l+32,
 // which are exactly the pair RoPE rotates).  q / k heads: RMSNorm over the
 // 64 values in the reference's order for a 64-wide row (rms_norm_kernel,
@@ -109,7 +110,7 @@ static __global__ void __launch_bounds__(256)
 // Written as bf16 in [B][heads][S][64] (one contiguous 128-byte row per
 // head and position), v heads converted only.
 static __global__ void __launch_bounds__(256)
-    qk_norm_rope_kernel(const float *__restrict__ qkv, const float *__restrict__ q_ln,
+    qk_norm_rope_kernel(const __nv_bfloat16 *__restrict__ qkv, const float *__restrict__ q_ln,
                         const float *__restrict__ k_ln, const float *__restrict__ cosv,
                         const float *__restrict__ sinv, int S, int Hq, int Hkv, float eps,
                         __nv_bfloat16 *__restrict__ q, __nv_bfloat16 *__restrict__ k,
@@ -119,14 +120,15 @@ static __global__ void __launch_bounds__(256)
   const int t = blockIdx.x, b = t / S, s = t - b * S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nh = Hq + 2 * Hkv;
-  const float *row = qkv + (size_t)t * nh * 64;
+  const __nv_bfloat16 *row = qkv + (size_t)t * nh * 64;
   for (int h = warp; h < nh; h += 8) {
-    const float x1 = row[h * 64 + lane], x2 = row[h * 64 + lane + 32];
+    const float x1 = __bfloat162float(row[h * 64 + lane]);
+    const float x2 = __bfloat162float(row[h * 64 + lane + 32]);
     __nv_bfloat16 *dst;
     if (h >= Hq + Hkv) {
       dst = v + (((size_t)b * Hkv + (h - Hq - Hkv)) * S + s) * 64;
-      dst[lane] = __float2bfloat16_rn(x1);
-      dst[lane + 32] = __float2bfloat16_rn(x2);
+      dst[lane] = row[h * 64 + lane];
+      dst[lane + 32] = row[h * 64 + lane + 32];
       continue;
     }
     float a = __fmul_rn(x1, x1), c = __fmul_rn(x2, x2);
@@ -344,7 +346,8 @@ static __global__ void __launch_bounds__(128)
 }
 
 // ------------------------------------------------------------ short conv
-// in_proj output ip: [T][3H] fp32 = (B | C | gate) per token; conv_w [H][3].
+// in_proj output ip: [T][3H] bf16 = (B | C | gate) per token (the projection
+// GEMM writes bf16: half the bytes of fp32 both ways); conv_w [H][3].
 // y[t][h] = C[t][h] * sum_k w[h][k] * Bx[t-2+k][h] over positions of the
 // same sequence (Bx = B * gate), the reference's FFMA chain from 0 in k order
 // (conv_transpose_split_kernel, causal_conv1d_kernel and
@@ -354,8 +357,8 @@ static __global__ void __launch_bounds__(128)
 constexpr int kConvRun = 16;
 constexpr int kConvL = 3;
 static __global__ void __launch_bounds__(128)
-    conv_glue_kernel(const float *__restrict__ ip, const float *__restrict__ cw, int S, int H,
-                     __nv_bfloat16 *__restrict__ y) {
+    conv_glue_kernel(const __nv_bfloat16 *__restrict__ ip, const float *__restrict__ cw, int S,
+                     int H, __nv_bfloat16 *__restrict__ y) {
   pdl_wait();
   pdl_trigger();
   const int h4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
@@ -367,10 +370,14 @@ static __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int k = 0; k < kConvL; ++k) w[c][k] = cw[(size_t)(h4 + c) * kConvL + k];
   const size_t ld = (size_t)3 * H;
-  const float *base = ip + (size_t)b * S * ld + h4;
+  const __nv_bfloat16 *base = ip + (size_t)b * S * ld + h4;
+  auto ld4 = [&](const __nv_bfloat16 *p) {  // 4 bf16 (8 bytes) as fp32
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+  };
   auto bx_at = [&](int s) {
-    const float4 bv = *reinterpret_cast<const float4 *>(base + (size_t)s * ld);
-    const float4 gv = *reinterpret_cast<const float4 *>(base + (size_t)s * ld + 2 * H);
+    const float4 bv = ld4(base + (size_t)s * ld);
+    const float4 gv = ld4(base + (size_t)s * ld + 2 * H);
     return make_float4(__fmul_rn(bv.x, gv.x), __fmul_rn(bv.y, gv.y), __fmul_rn(bv.z, gv.z),
                        __fmul_rn(bv.w, gv.w));
   };
@@ -396,7 +403,7 @@ static __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int k = 0; k < kConvL - 2; ++k) hist[k] = hist[k + 1];
     hist[kConvL - 2] = cur;
-    const float4 cv = *reinterpret_cast<const float4 *>(base + (size_t)s * ld + H);
+    const float4 cv = ld4(base + (size_t)s * ld + H);
     const uint2 out = make_uint2(pack_bf16(__fmul_rn(cv.x, acc[0]), __fmul_rn(cv.y, acc[1])),
                                  pack_bf16(__fmul_rn(cv.z, acc[2]), __fmul_rn(cv.w, acc[3])));
     *reinterpret_cast<uint2 *>(y + ((size_t)b * S + s) * H + h4) = out;

@@ -141,10 +141,14 @@ extern "C" b2_status b2_mlp_create(const b2_mlp_desc *desc, const float *w1, con
 
 extern "C" b2_status b2_mlp_forward(b2_mlp *m, const float *x, float *y, int T,
                                     b2_stream stream_) {
+  return mlp_forward_impl(m, x, y, T, reinterpret_cast<cudaStream_t>(stream_), false);
+}
+
+b2_status b2::mlp_forward_impl(b2_mlp *m, const float *x, float *y, int T, cudaStream_t s,
+                               bool accumulate) {
   if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   if (T == 0) return B2_OK;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   const int H = m->d.hidden, Ip = m->Ip;
   const bool f = m->tf32;
   const size_t es = f ? 4 : 2;
@@ -183,6 +187,7 @@ extern "C" b2_status b2_mlp_forward(b2_mlp *m, const float *x, float *y, int T,
   g2.out = y;
   g2.ldo = H;
   g2.status = m->status;
+  g2.accumulate = accumulate ? 1 : 0;
   const DensePlan p2 = plan_dense(T, H, m->sms, false, g2.num_k_blocks, splitk_cluster_caps(false));
   const CUtensorMap &tb2 = p2.b_box_rows == 64    ? m->tm_w2_64
                            : p2.b_box_rows == 128 ? m->tm_w2_128

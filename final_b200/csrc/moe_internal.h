@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <vector>
 
+#include "../../include/b2mlp.h"
 #include "../../include/b2moe.h"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
@@ -202,6 +203,7 @@ b2_status launch_gemm_splitk(const DensePlan &plan, const CUtensorMap &ta, const
   a.out = g.out;
   a.ldo = g.ldo;
   a.status = g.status;
+  a.accumulate = g.accumulate;
   const int n_tiles = EPI == kEpiSwiGLU ? g.N / 128 : (g.N + plan.bn - 1) / plan.bn;
   const int grid = a.m_tiles * n_tiles * plan.split;
   cudaLaunchConfig_t cfg = {};
@@ -335,7 +337,13 @@ b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *
 b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap &tm_a2,
                          void *inter, void *out, const GemmSched &sched, cudaStream_t s,
                          bool stage_marks = true);
-// y[t] = sum_k w[t,k] * m->sout[slot(t,k)]
-b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s);
+// y[t] = sum_k w[t,k] * m->sout[slot(t,k)]  (accumulate: y[t] += that sum)
+b2_status moe_combine_stage(b2_moe *m, float *y, int T, cudaStream_t s, bool accumulate = false);
+// The dense MLP's forward (mlp.cu); accumulate adds the MLP output into y.
+b2_status mlp_forward_impl(b2_mlp *m, const float *x, float *y, int T, cudaStream_t s,
+                           bool accumulate);
+// The whole single-GPU forward; accumulate adds the layer output into y.
+b2_status moe_forward_impl(b2_moe *m, const float *x, float *y, int T, const b2_moe_trace *tr,
+                           cudaStream_t s, bool accumulate);
 
 }  // namespace b2

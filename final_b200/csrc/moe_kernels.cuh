@@ -373,13 +373,14 @@ __global__ void __launch_bounds__(256)
 // combine_kernel: one block (256 threads) per token; thread handles 8 columns.
 // y[t,h] = fold over k of fma(out[slot_k,h], w[t,k], sum) from 0 -- the
 // reference's `sum += val * weight` in fixed k order (src/layer.cu:709-718).
-// Dropped pairs (slot -1) contribute nothing.
+// Dropped pairs (slot -1) contribute nothing.  With `accumulate` the sum is
+// added to y (y = y + sum, the decoder layer's residual add fused).
 // ---------------------------------------------------------------------------
 template <typename TIn>
 __global__ void __launch_bounds__(256)
     combine_kernel(const TIn *__restrict__ sorted_out, const int *__restrict__ token_slot,
                    const float *__restrict__ topk_w, int T, int H, int K,
-                   float *__restrict__ y) {
+                   float *__restrict__ y, int accumulate = 0) {
   const int t = blockIdx.x;
   __shared__ int ss[kMaxTopK];
   __shared__ float sw[kMaxTopK];
@@ -412,6 +413,13 @@ __global__ void __launch_bounds__(256)
       for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(v[i], wk, acc[i]);
     }
     float4 *dst = reinterpret_cast<float4 *>(y + (size_t)t * H + c);
+    if (accumulate) {
+      const float4 o0 = dst[0], o1 = dst[1];
+      acc[0] = __fadd_rn(o0.x, acc[0]); acc[1] = __fadd_rn(o0.y, acc[1]);
+      acc[2] = __fadd_rn(o0.z, acc[2]); acc[3] = __fadd_rn(o0.w, acc[3]);
+      acc[4] = __fadd_rn(o1.x, acc[4]); acc[5] = __fadd_rn(o1.y, acc[5]);
+      acc[6] = __fadd_rn(o1.z, acc[6]); acc[7] = __fadd_rn(o1.w, acc[7]);
+    }
     dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
