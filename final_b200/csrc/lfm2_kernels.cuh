@@ -54,7 +54,11 @@ static __global__ void __launch_bounds__(256)
 // FFMA, warps reduce by __shfl_down 16..1, warp 0 reduces the eight warp sums
 // by __shfl_down 4, 2, 1.  The division and square root are the IEEE ones
 // (no fast-math), so y equals the reference's bit for bit.
-static __global__ void __launch_bounds__(256)
+// NPT > 0: dim == 256 * NPT, the row stays in registers (all NPT loads in
+// flight at once, no second read); NPT == 0: any dim, two passes.  Both sum
+// in the same order.
+template <int NPT>
+__global__ void __launch_bounds__(256)
     add_rmsnorm_kernel(float *__restrict__ resid, const float *__restrict__ delta,
                        const float *__restrict__ w, int dim, int step, int off, int write_resid,
                        float eps, float *__restrict__ y32, __nv_bfloat16 *__restrict__ y16) {
@@ -65,13 +69,28 @@ static __global__ void __launch_bounds__(256)
   float *r = resid + row_in * dim;
   const float *dl = delta ? delta + row_in * dim : nullptr;
   float s = 0.0f;
-  for (int i = tid; i < dim; i += 256) {
-    float v = r[i];
+  float v[NPT > 0 ? NPT : 1];
+  if constexpr (NPT > 0) {
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) v[j] = r[tid + 256 * j];
     if (dl) {
-      v = __fadd_rn(v, dl[i]);
-      if (write_resid) r[i] = v;
+#pragma unroll
+      for (int j = 0; j < NPT; ++j) v[j] = __fadd_rn(v[j], dl[tid + 256 * j]);
+      if (write_resid)
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) r[tid + 256 * j] = v[j];
     }
-    s = __fmaf_rn(v, v, s);
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) s = __fmaf_rn(v[j], v[j], s);
+  } else {
+    for (int i = tid; i < dim; i += 256) {
+      float x = r[i];
+      if (dl) {
+        x = __fadd_rn(x, dl[i]);
+        if (write_resid) r[i] = x;
+      }
+      s = __fmaf_rn(x, x, s);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
@@ -80,20 +99,30 @@ static __global__ void __launch_bounds__(256)
   if (lane == 0) ws[warp] = s;
   __syncthreads();
   if (warp == 0) {
-    float v = lane < 8 ? ws[lane] : 0.0f;
+    float t = lane < 8 ? ws[lane] : 0.0f;
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
-    if (lane == 0) total = v;
+    for (int o = 4; o > 0; o >>= 1) t += __shfl_down_sync(0xffffffffu, t, o);
+    if (lane == 0) total = t;
   }
   __syncthreads();
   const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)dim), eps)));
   const size_t row_out = blockIdx.x;
-  for (int i = tid; i < dim; i += 256) {
-    float v = r[i];
-    if (dl && !write_resid) v = __fadd_rn(v, dl[i]);
-    const float o = __fmul_rn(__fmul_rn(v, rms), w[i]);
-    if (y32) y32[row_out * dim + i] = o;
-    if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+  if constexpr (NPT > 0) {
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+      const int i = tid + 256 * j;
+      const float o = __fmul_rn(__fmul_rn(v[j], rms), w[i]);
+      if (y32) y32[row_out * dim + i] = o;
+      if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+    }
+  } else {
+    for (int i = tid; i < dim; i += 256) {
+      float x = r[i];
+      if (dl && !write_resid) x = __fadd_rn(x, dl[i]);
+      const float o = __fmul_rn(__fmul_rn(x, rms), w[i]);
+      if (y32) y32[row_out * dim + i] = o;
+      if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+    }
   }
 }
 
