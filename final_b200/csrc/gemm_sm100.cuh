@@ -133,8 +133,11 @@ __device__ __forceinline__ void store_cols(TOut *dst, const float (&h)[32], int 
                                            bool vec_ok, bool add = false) {
   if (valid <= 0) return;
   if (add) {  // fp32 accumulate into C: C = C + result, element by element
-    if constexpr (sizeof(TOut) == 4)
-      for (int i = 0; i < 32 && i < valid; ++i) dst[i] = __fadd_rn(dst[i], h[i]);
+    if constexpr (sizeof(TOut) == 4) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)  // constant indices keep h in registers
+        if (i < valid) dst[i] = __fadd_rn(dst[i], h[i]);
+    }
     return;
   }
   if (valid >= 32 && vec_ok) {

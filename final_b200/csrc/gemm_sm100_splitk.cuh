@@ -78,10 +78,12 @@ __device__ __forceinline__ uint32_t part_off(int row, int u) {
 template <typename TOut>
 __device__ __forceinline__ void store4(TOut *dst, float a, float b, float c, float d, bool vec,
                                        int n_valid, bool add = false) {
+  const float v[4] = {a, b, c, d};
   if constexpr (sizeof(TOut) == 4) {
     if (add) {  // C = C + result
-      const float v[4] = {a, b, c, d};
-      for (int i = 0; i < 4 && i < n_valid; ++i) dst[i] = __fadd_rn(dst[i], v[i]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (i < n_valid) dst[i] = __fadd_rn(dst[i], v[i]);
       return;
     }
   }
@@ -92,8 +94,9 @@ __device__ __forceinline__ void store4(TOut *dst, float a, float b, float c, flo
       *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_bf16(a, b), pack_bf16(c, d));
     return;
   }
-  const float v[4] = {a, b, c, d};
-  for (int i = 0; i < 4 && i < n_valid; ++i) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // constant indices keep v in registers
+    if (i >= n_valid) break;
     if constexpr (sizeof(TOut) == 4) dst[i] = v[i];
     else dst[i] = __float2bfloat16_rn(v[i]);
   }
