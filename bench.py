@@ -57,6 +57,8 @@ def parse():
                    help="skip the full-model forward (config 5)")
     p.add_argument("--model-only", action="store_true",
                    help="only time the full-model forward (config 5)")
+    p.add_argument("--model-ep", choices=["none", "balanced", "owner"], default="balanced",
+                   help="with several GPUs, also time the expert-parallel model in this mode")
     p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
                    help="expert placement when --gpus > 1")
     p.add_argument("--gemm-configs", type=int, nargs=3, metavar=("M", "N", "K"),
@@ -437,6 +439,10 @@ def run_ours(args, rank, world, dev):
         fm = model_bench(dev, rank=rank, world=world)
         if rank == 0:
             out["full_model"] = fm
+        if world > 1 and args.model_ep != "none":
+            fm = model_bench(dev, rank=rank, world=world, ep=args.model_ep)
+            if rank == 0:
+                out["full_model_ep"] = fm
     if w_host is not None:
         out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
     return out
@@ -604,7 +610,7 @@ def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
 
 
 # ------------------------------------------------------------------ model
-def model_bench(dev, B=32, S=512, steps=5, warmup=3, rank=0, world=1):
+def model_bench(dev, B=32, S=512, steps=5, warmup=3, rank=0, world=1, ep=None):
     """Config 5: the whole LFM2-8B-A1B-shaped model (24 layers, random-init
     weights, vocab 65536) over batch 32 x seq 512 token ids uniform in
     [0, 65536): samples/s of the last-token logits, device-timed with inputs
@@ -612,13 +618,17 @@ def model_bench(dev, B=32, S=512, steps=5, warmup=3, rank=0, world=1):
     the logits copied back every step.  With several ranks every GPU holds a
     replica of the model (36 GB of its 180 GB) and runs its own batch of 32:
     no activation crosses NVLink; samples/s counts all ranks' samples over the
-    slowest rank's time (barrier before and after, max over ranks)."""
+    slowest rank's time (barrier before and after, max over ranks).  With
+    `ep` ("balanced" / "owner") the model is the expert-parallel one instead:
+    each rank still runs its own batch of 32, and every MoE layer exchanges
+    expert rows with the other ranks over NVLink."""
     import torch
     import torch.distributed as dist
     from final_b200 import launch_count
     from final_b200.lfm2 import LFM2Model, model_flop, synthetic_weights
     t0 = time.time()
-    model = LFM2Model(synthetic_weights(dev, seed=11), max_batch=B, max_seq=S, device=dev)
+    kw = {} if ep is None else dict(expert_parallel=ep, world=world, rank=rank)
+    model = LFM2Model(synthetic_weights(dev, seed=11), max_batch=B, max_seq=S, device=dev, **kw)
     torch.cuda.empty_cache()
     build_s = time.time() - t0
     g = torch.Generator(device=dev).manual_seed(12 + 1000 * rank)
@@ -676,7 +686,9 @@ def model_bench(dev, B=32, S=512, steps=5, warmup=3, rank=0, world=1):
     pk = peaks()
     out = {"workload": "lfm2_8b_a1b_shaped_forward", "batch_per_gpu": B, "seq_len": S,
            "layers": 24, "vocab": 65536, "n_gpus": world,
-           "parallelism": "single" if world == 1 else f"replica per GPU x{world}",
+           "parallelism": ("single" if world == 1 and ep is None else
+                           f"replica per GPU x{world}" if ep is None else
+                           f"expert-parallel MoE layers ({ep}) x{world}"),
            "scaling": "weak", "weights": "random init (bf16 projections / experts from fp32)",
            "samples_per_s": B * world / (ms / 1e3), "tokens_per_s": B * S * world / (ms / 1e3),
            "ms_per_forward": ms, "tflops_per_gpu": flop / (ms / 1e3) / 1e12,
@@ -840,6 +852,11 @@ def main():
         fm = model_bench(dev, steps=args.steps, warmup=args.warmup, rank=rank, world=world)
         if rank == 0:
             print(json.dumps(fm), flush=True)
+        if world > 1 and args.model_ep != "none":
+            fm = model_bench(dev, steps=args.steps, warmup=args.warmup, rank=rank, world=world,
+                             ep=args.model_ep)
+            if rank == 0:
+                print(json.dumps(fm), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return 0

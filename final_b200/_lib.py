@@ -30,8 +30,8 @@ EXPORTED = (
     "b2_rmsnorm", "b2_add_rmsnorm", "b2_rope_tables", "b2_embed",
     "b2_attn_create", "b2_attn_forward", "b2_attn_destroy",
     "b2_conv_create", "b2_conv_forward", "b2_conv_destroy",
-    "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex", "b2_lfm2_get_status",
-    "b2_lfm2_device_bytes", "b2_lfm2_destroy",
+    "b2_lfm2_create", "b2_lfm2_create_ep", "b2_lfm2_set_timeout", "b2_lfm2_forward",
+    "b2_lfm2_forward_ex", "b2_lfm2_get_status", "b2_lfm2_device_bytes", "b2_lfm2_destroy",
     # include/b2loader.h
     "b2_loader_open", "b2_loader_num_tensors", "b2_loader_name", "b2_loader_tensor",
     "b2_loader_weight", "b2_loader_close",
@@ -166,6 +166,9 @@ def load(path: Path | None = None):
     lib.b2_conv_forward.argtypes = [vp, vp, vp, i, i, vp]
     lib.b2_conv_destroy.argtypes = [vp]
     lib.b2_lfm2_create.argtypes = [C.POINTER(Lfm2Desc), WEIGHT_FN, vp, i, vp, C.POINTER(vp)]
+    lib.b2_lfm2_create_ep.argtypes = [C.POINTER(Lfm2Desc), WEIGHT_FN, vp, i, i, i, vp, i, vp,
+                                      C.POINTER(vp)]
+    lib.b2_lfm2_set_timeout.argtypes = [vp, C.c_double]
     lib.b2_lfm2_forward.argtypes = [vp, vp, i, i, vp, vp]
     lib.b2_lfm2_forward_ex.argtypes = [vp, vp, i, i, vp, vp, vp]
     lib.b2_lfm2_get_status.argtypes = [vp, vp, C.POINTER(i)]
@@ -174,8 +177,9 @@ def load(path: Path | None = None):
     lib.b2_lfm2_destroy.argtypes = [vp]
     for name in ("b2_rmsnorm", "b2_add_rmsnorm", "b2_rope_tables", "b2_embed", "b2_attn_create",
                  "b2_attn_forward", "b2_attn_destroy", "b2_conv_create", "b2_conv_forward",
-                 "b2_conv_destroy", "b2_lfm2_create", "b2_lfm2_forward", "b2_lfm2_forward_ex",
-                 "b2_lfm2_get_status", "b2_lfm2_destroy"):
+                 "b2_conv_destroy", "b2_lfm2_create", "b2_lfm2_create_ep", "b2_lfm2_set_timeout",
+                 "b2_lfm2_forward", "b2_lfm2_forward_ex", "b2_lfm2_get_status",
+                 "b2_lfm2_destroy"):
         getattr(lib, name).restype = i
     lib.b2_loader_open.argtypes = [C.c_char_p, C.POINTER(vp)]
     lib.b2_loader_open.restype = i

@@ -209,11 +209,20 @@ extern "C" b2_status b2_ep_plan_compute(int G, int r, int E, int mode, const int
 // the forward's sequence number, so they never need resetting.
 static constexpr int kFlagDispatch = 0, kFlagReturn = 1;
 
+// The communicator of one or more layers.  A model's MoE layers share one:
+// all of their collectives are issued on the model's stream in layer order,
+// so every rank meets them in the same order.  When a layer aborts it (a lost
+// peer), every layer that shares it sees `ok == false`.
+struct EpComm {
+  ncclComm_t comm = nullptr;  // count all-gather (the per-forward barrier) and set-up
+  bool ok = false;
+  int refs = 1;
+};
+
 struct b2_ep {
   b2_moe *moe = nullptr;
   int world = 1, rank = 0, mode = 0, E = 0, n_wexp = 0;
-  ncclComm_t comm = nullptr;  // count all-gather (the per-forward barrier) and set-up
-  bool comm_ok = false;
+  EpComm *cm = nullptr;
   cudaStream_t st_d = nullptr, st_r = nullptr;  // copy-engine streams: dispatch / return
   std::vector<cudaEvent_t> ev_out;               // per exchange step
   cudaEvent_t ev_ready = nullptr, ev_ret = nullptr;
@@ -274,9 +283,9 @@ extern "C" b2_status b2_ep_unique_id(void *id_out) {
 }
 
 static void ep_abort(b2_ep *ep) {
-  if (ep->comm) nccl().CommAbort(ep->comm);
-  ep->comm = nullptr;
-  ep->comm_ok = false;
+  if (ep->cm->comm) nccl().CommAbort(ep->cm->comm);
+  ep->cm->comm = nullptr;
+  ep->cm->ok = false;
 }
 
 // Wait for `s` with a bound; abort the communicator if a peer is lost.
@@ -290,7 +299,7 @@ static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
       return B2_ERR_CUDA;
     }
     ncclResult_t ae = ncclSuccess;
-    if (nccl().CommGetAsyncError(ep->comm, &ae) != ncclSuccess || ae != ncclSuccess) {
+    if (nccl().CommGetAsyncError(ep->cm->comm, &ae) != ncclSuccess || ae != ncclSuccess) {
       ep_abort(ep);
       return B2_ERR_COMM;
     }
@@ -308,10 +317,10 @@ static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
 
 extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   if (!ep) return B2_OK;
-  if (ep->comm_ok && ep->world > 1 && ep->moe) {
+  if (ep->cm && ep->cm->ok && ep->world > 1 && ep->moe && ep->d_cnt_all) {
     // every rank stops using the others' memory before anyone unmaps it
     cudaStream_t s = ep->st_d;
-    if (nccl().AllGather(ep->moe->counts, ep->d_cnt_all, ep->E, ncclInt32, ep->comm, s) ==
+    if (nccl().AllGather(ep->moe->counts, ep->d_cnt_all, ep->E, ncclInt32, ep->cm->comm, s) ==
         ncclSuccess)
       bounded_sync(ep, s);
   }
@@ -323,11 +332,14 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
     if (p) cudaIpcCloseMemHandle(p);
   for (uint64_t *p : ep->peer_flags)
     if (p) cudaIpcCloseMemHandle(p);
-  if (ep->comm) {
-    if (ep->comm_ok)
-      nccl().CommDestroy(ep->comm);
-    else
-      nccl().CommAbort(ep->comm);
+  if (ep->cm && --ep->cm->refs == 0) {
+    if (ep->cm->comm) {
+      if (ep->cm->ok)
+        nccl().CommDestroy(ep->cm->comm);
+      else
+        nccl().CommAbort(ep->cm->comm);
+    }
+    delete ep->cm;
   }
   for (cudaEvent_t e : ep->ev_out) cudaEventDestroy(e);
   if (ep->ev_ready) cudaEventDestroy(ep->ev_ready);
@@ -343,14 +355,15 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   return B2_OK;
 }
 
-extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
-                                  const void *unique_id, int mode, const float *const *w1,
-                                  const float *const *w2, const float *const *w3,
-                                  const float *gate, const float *bias, int weights_on_host,
-                                  b2_stream stream_, b2_ep **out) {
-  if (!desc || !unique_id || !out || world < 1 || world > B2_EP_MAX_WORLD || rank < 0 ||
-      rank >= world)
+b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
+                            const void *unique_id, b2_ep *share, int mode,
+                            const float *const *w1, const float *const *w2,
+                            const float *const *w3, const float *gate, const float *bias,
+                            int weights_on_host, b2_stream stream_, b2_ep **out) {
+  if (!desc || (!unique_id && !share) || !out || world < 1 || world > B2_EP_MAX_WORLD ||
+      rank < 0 || rank >= world)
     return B2_ERR_INVALID;
+  if (share && (share->world != world || share->rank != rank)) return B2_ERR_INVALID;
   if (mode != B2_EP_OWNER && mode != B2_EP_BALANCED) return B2_ERR_INVALID;
   const int E = desc->num_experts;
   if (mode == B2_EP_OWNER && E % world != 0) return B2_ERR_INVALID;
@@ -416,13 +429,20 @@ extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
     if (cudaEventCreateWithFlags(&ep->ev_out[k], cudaEventDisableTiming) != cudaSuccess)
       return fail(B2_ERR_CUDA);
   if (cudaStreamSynchronize(stream) != cudaSuccess) return fail(B2_ERR_CUDA);
-  ncclUniqueId id;
-  memcpy(&id, unique_id, sizeof(id));
-  if (nccl().CommInitRank(&ep->comm, world, id, rank) != ncclSuccess) {
-    ep->comm = nullptr;
-    return fail(B2_ERR_COMM);
+  if (share) {
+    ep->cm = share->cm;
+    ++ep->cm->refs;
+    if (!ep->cm->ok) return fail(B2_ERR_COMM);
+  } else {
+    ep->cm = new EpComm();
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof(id));
+    if (nccl().CommInitRank(&ep->cm->comm, world, id, rank) != ncclSuccess) {
+      ep->cm->comm = nullptr;
+      return fail(B2_ERR_COMM);
+    }
+    ep->cm->ok = true;
   }
-  ep->comm_ok = true;
   ep->plans.resize(world);
   // share IPC handles of the receive buffer, sout and the flag words
   ep->peer_recv.assign(world, nullptr);
@@ -444,7 +464,7 @@ extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
                         cudaMemcpyHostToDevice, stream) != cudaSuccess)
       return fail(B2_ERR_CUDA);
     if (nccl().AllGather(static_cast<char *>(d_h) + 3 * kH * rank, d_h, 3 * kH, ncclUint8,
-                         ep->comm, stream) != ncclSuccess)
+                         ep->cm->comm, stream) != ncclSuccess)
       return fail(B2_ERR_COMM);
     if (cudaMemcpyAsync(all.data(), d_h, 3 * kH * world, cudaMemcpyDeviceToHost, stream) !=
         cudaSuccess)
@@ -470,6 +490,16 @@ extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
   }
   *out = ep;
   return B2_OK;
+}
+
+extern "C" b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
+                                  const void *unique_id, int mode, const float *const *w1,
+                                  const float *const *w2, const float *const *w3,
+                                  const float *gate, const float *bias, int weights_on_host,
+                                  b2_stream stream, b2_ep **out) {
+  if (!unique_id) return B2_ERR_INVALID;
+  return ep_create_impl(desc, world, rank, unique_id, nullptr, mode, w1, w2, w3, gate, bias,
+                        weights_on_host, stream, out);
 }
 
 // GEMM schedule of the segments that came from `src` (rows of the receive
@@ -498,13 +528,12 @@ static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self
   return n;
 }
 
-extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
-                                   b2_stream stream_) {
+b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaStream_t s,
+                             bool accumulate) {
   if (!ep || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
-  if (!ep->comm_ok) return B2_ERR_COMM;
+  if (!ep->cm->ok) return B2_ERR_COMM;
   b2_moe *m = ep->moe;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
   const int E = ep->E, G = ep->world, r = ep->rank, H = m->d.hidden;
   const size_t rb = (m->tf32 ? 4 : 2) * (size_t)H;  // bytes per row
   const uint64_t timeout_ns = (uint64_t)(ep->timeout_s * 1e9);
@@ -520,7 +549,7 @@ extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
   // 2. count matrix -> host.  The all-gather completes only after every rank's
   // previous forward finished on its stream, so after this point every peer
   // buffer written below is free for this forward.
-  B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->comm, s));
+  B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->cm->comm, s));
   B2_CUDA(cudaMemcpyAsync(ep->h_cnt_all, ep->d_cnt_all, sizeof(int32_t) * G * E,
                           cudaMemcpyDeviceToHost, s));
   B2_RETURN_IF(bounded_sync(ep, s));
@@ -620,11 +649,16 @@ extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
   }
   // 6. local k-ordered combine
   if (T > 0) {
-    B2_RETURN_IF(moe_combine_stage(m, y, T, s));
+    B2_RETURN_IF(moe_combine_stage(m, y, T, s, accumulate));
   } else {
     for (int i = 0; i < 2; ++i) prof_mark(m, s);
   }
   return B2_OK;
+}
+
+extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
+                                   b2_stream stream) {
+  return ep_forward_impl(ep, x, y, T, reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 extern "C" b2_status b2_ep_set_timeout(b2_ep *ep, double seconds) {

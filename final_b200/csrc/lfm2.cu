@@ -467,6 +467,12 @@ struct Layer {
   float *op_norm = nullptr, *ffn_norm = nullptr;
   b2_moe *moe = nullptr;
   b2_mlp *mlp = nullptr;
+  b2_ep *ep = nullptr;  // expert-parallel MoE (models made by b2_lfm2_create_ep)
+};
+
+struct EpCfg {
+  int world = 1, rank = 0, mode = 0;
+  const void *unique_id = nullptr;
 };
 }  // namespace
 
@@ -484,6 +490,8 @@ struct b2_lfm2 {
   __nv_bfloat16 *lastb = nullptr;  // [max_batch][H]
   CUtensorMap tm_lastb;
   int *status = nullptr;
+  int world = 1, rank = 0;  // expert-parallel group (world 1: a single-GPU model)
+  bool ep = false;
 };
 
 extern "C" b2_status b2_lfm2_destroy(b2_lfm2 *m) {
@@ -491,9 +499,11 @@ extern "C" b2_status b2_lfm2_destroy(b2_lfm2 *m) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(m->device);
+  // expert-parallel layers are destroyed collectively, in the same order on every rank
   for (Layer &l : m->layers) {
     if (l.moe) b2_moe_destroy(l.moe);
     if (l.mlp) b2_mlp_destroy(l.mlp);
+    if (l.ep) b2_ep_destroy(l.ep);
   }
   m->mem.release();
   cudaSetDevice(prev);
@@ -514,8 +524,9 @@ struct Fetch {
 };
 }  // namespace
 
-extern "C" b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
-                                    int weights_on_host, b2_stream stream, b2_lfm2 **out) {
+static b2_status lfm2_create_impl(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
+                                  int weights_on_host, b2_stream stream, const EpCfg *ep,
+                                  b2_lfm2 **out) {
   if (!desc || !get || !out) return B2_ERR_INVALID;
   *out = nullptr;
   const b2_lfm2_desc &d = *desc;
@@ -537,6 +548,11 @@ extern "C" b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, 
   b2_lfm2 *m = new b2_lfm2();
   m->d = d;
   m->sms = di.sms;
+  if (ep) {
+    m->ep = true;
+    m->world = ep->world;
+    m->rank = ep->rank;
+  }
   cudaGetDevice(&m->device);
   Fetch f{get, ctx, {}};
   Stager sg;
@@ -634,26 +650,68 @@ extern "C" b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, 
       B2_TRY(b2_mlp_create(&md, w1, w2, w3, weights_on_host, stream, &L.mlp));
     } else {
       const int E = d.num_experts, I = d.moe_inter;
-      std::vector<const float *> w1(E), w2(E), w3(E);
-      for (int e = 0; e < E; ++e) {
-        const std::string x = ff + "experts." + std::to_string(e) + ".";
-        w1[e] = f(x + "w1.weight", (int64_t)I * H);
-        w2[e] = f(x + "w2.weight", (int64_t)H * I);
-        w3[e] = f(x + "w3.weight", (int64_t)I * H);
-        if (!w1[e] || !w2[e] || !w3[e]) return fail(B2_ERR_INVALID);
+      // an expert-parallel owner fetches only its experts [rank*E/world, ...)
+      const bool owner = ep && ep->mode == B2_EP_OWNER;
+      const int e0 = owner ? ep->rank * (E / ep->world) : 0;
+      const int ne = owner ? E / ep->world : E;
+      std::vector<const float *> w1(ne), w2(ne), w3(ne);
+      for (int j = 0; j < ne; ++j) {
+        const std::string x = ff + "experts." + std::to_string(e0 + j) + ".";
+        w1[j] = f(x + "w1.weight", (int64_t)I * H);
+        w2[j] = f(x + "w2.weight", (int64_t)H * I);
+        w3[j] = f(x + "w3.weight", (int64_t)I * H);
+        if (!w1[j] || !w2[j] || !w3[j]) return fail(B2_ERR_INVALID);
       }
       const float *gate = f(ff + "gate.weight", (int64_t)E * H);
       const float *bias = d.use_expert_bias ? f(ff + "expert_bias", E) : nullptr;
       if (!gate || (d.use_expert_bias && !bias)) return fail(B2_ERR_INVALID);
       b2_moe_desc md{H, I, E, d.top_k, (int)maxT, d.routed_scale, d.use_expert_bias ? 1 : 0,
                      d.dtype};
-      B2_TRY(b2_moe_create(&md, w1.data(), w2.data(), w3.data(), gate, bias, weights_on_host,
-                           stream, &L.moe));
+      if (ep) {
+        // the first MoE layer creates the communicator, the others share it
+        b2_ep *first = nullptr;
+        for (int j = 0; j < i && !first; ++j) first = m->layers[j].ep;
+        B2_TRY(ep_create_impl(&md, ep->world, ep->rank, ep->unique_id, first, ep->mode,
+                              w1.data(), w2.data(), w3.data(), gate, bias, weights_on_host,
+                              stream, &L.ep));
+      } else {
+        B2_TRY(b2_moe_create(&md, w1.data(), w2.data(), w3.data(), gate, bias, weights_on_host,
+                             stream, &L.moe));
+      }
     }
   }
   B2_TRY(cudaStreamSynchronize(s) == cudaSuccess ? B2_OK : B2_ERR_CUDA);
 #undef B2_TRY
   *out = m;
+  return B2_OK;
+}
+
+extern "C" b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
+                                    int weights_on_host, b2_stream stream, b2_lfm2 **out) {
+  return lfm2_create_impl(desc, get, ctx, weights_on_host, stream, nullptr, out);
+}
+
+extern "C" b2_status b2_lfm2_create_ep(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
+                                       int weights_on_host, int world, int rank,
+                                       const void *unique_id, int mode, b2_stream stream,
+                                       b2_lfm2 **out) {
+  if (!unique_id || world < 1 || world > B2_EP_MAX_WORLD || rank < 0 || rank >= world ||
+      (mode != B2_EP_OWNER && mode != B2_EP_BALANCED))
+    return B2_ERR_INVALID;
+  if (!desc || desc->num_dense_layers >= desc->num_layers) return B2_ERR_INVALID;
+  if (mode == B2_EP_OWNER && desc->num_experts % world) return B2_ERR_INVALID;
+  EpCfg ep;
+  ep.world = world;
+  ep.rank = rank;
+  ep.mode = mode;
+  ep.unique_id = unique_id;
+  return lfm2_create_impl(desc, get, ctx, weights_on_host, stream, &ep, out);
+}
+
+extern "C" b2_status b2_lfm2_set_timeout(b2_lfm2 *m, double seconds) {
+  if (!m || !(seconds > 0)) return B2_ERR_INVALID;
+  for (Layer &L : m->layers)
+    if (L.ep) B2_RETURN_IF(b2_ep_set_timeout(L.ep, seconds));
   return B2_OK;
 }
 
@@ -683,6 +741,8 @@ static b2_status lfm2_forward_impl(b2_lfm2 *m, const int32_t *ids, int B, int S,
     B2_RETURN_IF(norm_launch(m->resid, nullptr, L.ffn_norm, T, H, 1, 0, 0, eps, m->hn, nullptr, s));
     if (L.moe)
       B2_RETURN_IF(moe_forward_impl(L.moe, m->hn, m->resid, T, nullptr, s, true));
+    else if (L.ep)
+      B2_RETURN_IF(ep_forward_impl(L.ep, m->hn, m->resid, T, s, true));
     else
       B2_RETURN_IF(mlp_forward_impl(L.mlp, m->hn, m->resid, T, s, true));
     if (hidden_out)
@@ -698,11 +758,18 @@ static b2_status lfm2_forward_impl(b2_lfm2 *m, const int32_t *ids, int B, int S,
 extern "C" b2_status b2_lfm2_forward_ex(b2_lfm2 *m, const int32_t *ids, int batch, int seq_len,
                                         float *logits, float *hidden_out, b2_stream stream) {
   if (!m || batch < 0 || seq_len < 0) return B2_ERR_INVALID;
-  if (batch == 0 || seq_len == 0) return B2_OK;
-  if (!ids || !logits) return B2_ERR_INVALID;
   if (batch > m->d.max_batch || seq_len > m->d.max_seq) return B2_ERR_CAPACITY;
-  return lfm2_forward_impl(m, ids, batch, seq_len, logits, hidden_out,
-                           reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (batch == 0 || seq_len == 0) {
+    // an expert-parallel rank without tokens still takes part in every
+    // layer's exchange, in layer order
+    if (m->ep)
+      for (Layer &L : m->layers)
+        if (L.ep) B2_RETURN_IF(ep_forward_impl(L.ep, nullptr, nullptr, 0, s, true));
+    return B2_OK;
+  }
+  if (!ids || !logits) return B2_ERR_INVALID;
+  return lfm2_forward_impl(m, ids, batch, seq_len, logits, hidden_out, s);
 }
 
 extern "C" b2_status b2_lfm2_forward(b2_lfm2 *m, const int32_t *ids, int batch, int seq_len,
@@ -721,6 +788,7 @@ extern "C" b2_status b2_lfm2_get_status(b2_lfm2 *m, b2_stream stream, int *devic
     int lv = 0;
     if (L.moe) b2_moe_get_status(L.moe, stream, &lv);
     if (L.mlp) b2_mlp_get_status(L.mlp, stream, &lv);
+    if (L.ep) b2_moe_get_status(b2_ep_layer(L.ep), stream, &lv);
     if (!v) v = lv;
   }
   *device_status = v;
@@ -733,6 +801,7 @@ extern "C" size_t b2_lfm2_device_bytes(const b2_lfm2 *m) {
   for (const Layer &L : m->layers) {
     if (L.moe) b += b2_moe_device_bytes(L.moe);
     if (L.mlp) b += b2_mlp_device_bytes(L.mlp);
+    if (L.ep) b += b2_moe_device_bytes(b2_ep_layer(L.ep));
   }
   return b;
 }

@@ -13,6 +13,7 @@
 
 #include "../../include/b2mlp.h"
 #include "../../include/b2moe.h"
+#include "../../include/b2moe_ep.h"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
 #include "gemm_sm100_splitk.cuh"
@@ -345,5 +346,17 @@ b2_status mlp_forward_impl(b2_mlp *m, const float *x, float *y, int T, cudaStrea
 // The whole single-GPU forward; accumulate adds the layer output into y.
 b2_status moe_forward_impl(b2_moe *m, const float *x, float *y, int T, const b2_moe_trace *tr,
                            cudaStream_t s, bool accumulate);
+
+// Expert-parallel layer (ep.cu).  With `share` the new layer uses share's
+// communicator instead of creating one from unique_id (collective either way);
+// the communicator lives until the last layer using it is destroyed.
+b2_status ep_create_impl(const b2_moe_desc *desc, int world, int rank, const void *unique_id,
+                         b2_ep *share, int mode, const float *const *w1,
+                         const float *const *w2, const float *const *w3, const float *gate,
+                         const float *bias, int weights_on_host, b2_stream stream,
+                         b2_ep **out);
+// b2_ep_forward; accumulate adds the layer output into y.
+b2_status ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaStream_t s,
+                          bool accumulate);
 
 }  // namespace b2

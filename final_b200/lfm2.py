@@ -10,6 +10,7 @@ compute goes through the C ABI of include/b2lfm2.h; errors raise B2Error.
 from __future__ import annotations
 
 import ctypes as C
+import zlib
 from typing import Callable, Dict, Optional
 
 import numpy as np
@@ -155,13 +156,22 @@ class LFM2Model(_Handle):
     fp32 torch tensor on the device, or a numpy array with
     ``weights_on_host=True``) or None when the model has no such tensor; the
     returned objects are kept alive until construction ends.  Other
-    keywords override the reference configuration (``CONFIG``)."""
+    keywords override the reference configuration (``CONFIG``).
+
+    ``expert_parallel`` ("balanced" or "owner") builds the expert-parallel
+    model instead (b2_lfm2_create_ep): one rank per GPU, every MoE layer an
+    expert-parallel layer over ``world`` ranks, all of them sharing one NCCL
+    communicator made from ``uid`` (created on rank 0 and broadcast over the
+    default torch.distributed group when None).  Construction, forward and
+    close are collective."""
     _destroy = "b2_lfm2_destroy"
 
     def __init__(self, weights: Callable[[str, int], object], *, max_batch: int, max_seq: int,
                  weights_on_host: bool = False, layer_types=LAYER_TYPES, dtype: str = "bf16",
                  device: Optional[torch.device] = None,
-                 stream: Optional[torch.cuda.Stream] = None, **cfg):
+                 stream: Optional[torch.cuda.Stream] = None,
+                 expert_parallel: Optional[str] = None, world: Optional[int] = None,
+                 rank: Optional[int] = None, uid: Optional[bytes] = None, **cfg):
         self.lib = _lib.load()
         c = dict(CONFIG)
         c.update(cfg)
@@ -205,10 +215,32 @@ class LFM2Model(_Handle):
             cb, ctx = WEIGHT_FN(get), None
         h = C.c_void_p()
         self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.expert_parallel = expert_parallel
         with torch.cuda.device(self.device):
-            check(self.lib.b2_lfm2_create(C.byref(d), cb, ctx, int(weights_on_host),
-                                          C.c_void_p(_stream_ptr(stream)), C.byref(h)),
-                  "b2_lfm2_create")
+            if expert_parallel is None:
+                check(self.lib.b2_lfm2_create(C.byref(d), cb, ctx, int(weights_on_host),
+                                              C.c_void_p(_stream_ptr(stream)), C.byref(h)),
+                      "b2_lfm2_create")
+            else:
+                from .ep import MODES, unique_id
+                import torch.distributed as dist
+                if world is None:
+                    world = dist.get_world_size() if dist.is_initialized() else 1
+                if rank is None:
+                    rank = dist.get_rank() if dist.is_initialized() else 0
+                if uid is None:
+                    if world == 1:
+                        uid = unique_id()
+                    else:
+                        obj = [unique_id() if rank == 0 else None]
+                        dist.broadcast_object_list(obj, src=0)
+                        uid = obj[0]
+                self.world, self.rank = world, rank
+                idbuf = C.create_string_buffer(bytes(uid), len(uid))
+                check(self.lib.b2_lfm2_create_ep(C.byref(d), cb, ctx, int(weights_on_host),
+                                                 world, rank, idbuf, MODES[expert_parallel],
+                                                 C.c_void_p(_stream_ptr(stream)), C.byref(h)),
+                      "b2_lfm2_create_ep")
         keep.clear()
         self._h = h
 
@@ -261,13 +293,15 @@ def synthetic_weights(device, seed: int = 0):
     fp32 tensors on `device`: embedding N(0,1); RMSNorm weights N(1,0.1);
     conv taps N(0,0.3); projections, experts, router and expert bias
     N(0,0.02); no separate lm_head.weight (tied, as the reference model).
+    Each tensor's values depend only on (seed, name), so a rank that fetches
+    a subset (an expert-parallel owner) gets the same tensors as a full model.
     For benchmarks: no checkpoint is needed."""
     g = torch.Generator(device=device)
-    g.manual_seed(seed)
 
     def get(name: str, numel: int):
         if name == "lm_head.weight":
             return None
+        g.manual_seed((seed << 32) ^ zlib.crc32(name.encode()))
         last = name.split(".")[-2] if name.count(".") else name
         if name == "embed_tokens.weight":
             mean, std = 0.0, 1.0

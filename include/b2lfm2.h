@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "b2moe.h"
+#include "b2moe_ep.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -148,6 +149,29 @@ typedef struct b2_lfm2 b2_lfm2;
  * 172-179), rotary tables for max_seq positions.  Synchronises stream. */
 b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
                          int weights_on_host, b2_stream stream, b2_lfm2 **out);
+
+/* The expert-parallel model over `world` GPUs, one process (rank) per GPU;
+ * replaces the 24-stage pipeline of init_gpu_pipeline / worker_stage
+ * (src/model.cu:235-562), which moves the whole residual stream between
+ * GPUs at stage boundaries.  Here every rank runs the embedding, attention /
+ * conv blocks, dense MLPs and LM head on its own batch, and each MoE layer is
+ * a b2_ep layer (include/b2moe_ep.h) in `mode`: only expert rows cross NVLink.
+ * In B2_EP_OWNER mode `get` is asked only for this rank's experts
+ * [rank*E/world, (rank+1)*E/world).  All MoE layers share one NCCL
+ * communicator made from unique_id (b2_ep_unique_id on rank 0, shared by the
+ * caller).  Collective: create, every forward and destroy are called by all
+ * ranks in the same order; a rank with no tokens calls b2_lfm2_forward with
+ * batch 0 and still takes part in every layer's exchange.  Each forward
+ * synchronises `stream` once per MoE layer (the count all-gather of
+ * b2_ep_forward); logits are bit-identical to b2_lfm2_create's model on the
+ * same tokens. */
+b2_status b2_lfm2_create_ep(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
+                            int weights_on_host, int world, int rank, const void *unique_id,
+                            int mode, b2_stream stream, b2_lfm2 **out);
+
+/* Host-side bound (seconds) on every wait for peers of an expert-parallel
+ * model (default 60); B2_OK and no effect on a single-GPU model. */
+b2_status b2_lfm2_set_timeout(b2_lfm2 *model, double seconds);
 
 /* Replaces LFM2Model::forward(sample_idx, batch, ids, seq_len, out) as the
  * pipeline computes it (src/model.cu:385-548): logits[batch][vocab] (fp32,
