@@ -312,7 +312,10 @@ def run_ours(args, rank, world, dev):
     torch.cuda.synchronize()
     layer.profile(False)
     stage_ms, nfw = layer.profile_read()
+    timeline = None
     if world > 1:
+        timeline = [None] * world
+        dist.all_gather_object(timeline, layer.timeline())
         dist.barrier()
     st = layer.device_status()
     if st != 0:
@@ -419,6 +422,7 @@ def run_ours(args, rank, world, dev):
         "grouped_gemm_tflops": gemm_flop / ((w13_ms + w2_ms) / 1e3) / 1e12,
         "frac_of_bf16_peak_layer": flop / (ms / args.steps / 1e3) / 1e12 / pk["bf16"],
         "stages_ms_per_step": {k: v / max(nfw, 1) for k, v in stage_ms.items()},
+        **({"ep_timeline_us": timeline} if timeline else {}),
         "roofline": {"kernel": "gemm_pair_kernel<SwiGLU,bf16> (W1||W3 grouped GEMM, CTA pairs)",
                      "bound": "tensor", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s",

@@ -23,6 +23,7 @@ EXPORTED = (
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
     "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy", "b2_flag_wait",
+    "b2_ep_profile_timeline",
     # include/b2mlp.h
     "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_device_bytes",
     "b2_mlp_destroy",
@@ -144,6 +145,8 @@ def load(path: Path | None = None):
     lib.b2_ep_set_timeout.argtypes = [vp, C.c_double]
     lib.b2_flag_wait.argtypes = [vp, vp, i, C.c_uint64, C.c_double, vp, vp]
     lib.b2_ep_last_plan.argtypes = [vp, C.POINTER(EpPlan)]
+    lib.b2_ep_profile_timeline.argtypes = [vp, i, C.POINTER(i), C.POINTER(C.c_float),
+                                           C.POINTER(i)]
     lib.b2_ep_layer.argtypes = [vp]
     lib.b2_ep_layer.restype = vp
     lib.b2_ep_destroy.argtypes = [vp]
@@ -204,6 +207,7 @@ def load(path: Path | None = None):
                  "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc",
                  "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
                  "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy", "b2_flag_wait",
+                 "b2_ep_profile_timeline",
                  "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_destroy"):
         getattr(lib, name).restype = i
     _lib = lib

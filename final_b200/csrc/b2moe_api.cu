@@ -269,7 +269,7 @@ b2_status moe_create_impl(const b2_moe_desc *desc, int n_wexp, const float *cons
 }
 
 b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *tr,
-                          cudaStream_t s) {
+                          cudaStream_t s, bool with_scatter) {
   const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden;
   const int nb = (T + kRouteTB - 1) / kRouteTB;
   prof_mark(m, s);
@@ -281,6 +281,12 @@ b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *
   B2_RETURN_IF(launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, s, (const int *)m->block_counts, nb,
                           E, (int)kPairBM, m->counts, m->offsets, m->mtile, m->block_base));
   prof_mark(m, s);
+  return with_scatter ? moe_scatter_stage(m, x, T, s) : B2_OK;
+}
+
+b2_status moe_scatter_stage(b2_moe *m, const float *x, int T, cudaStream_t s) {
+  const int E = m->d.num_experts, K = m->d.top_k, H = m->d.hidden;
+  const int nb = (T + kRouteTB - 1) / kRouteTB;
   if (m->tf32)
     B2_RETURN_IF(launch_pdl(scatter_kernel<float>, dim3(nb), dim3(scatter_threads(K)), 0, s, x,
                             (const int *)m->topk_idx, (const float *)m->topk_w,

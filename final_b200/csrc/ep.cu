@@ -1,10 +1,12 @@
 // ep.cu -- expert-parallel MoE layer (include/b2moe_ep.h).
 //
 // Per forward on every rank:
-//   1. route / scan / scatter the local tokens (moe_route_stage): rows in
-//      expert order in sorted_x, per-expert counts on the device;
-//   2. all-gather the [world][E] count matrix; one bounded host wait, then every
-//      rank computes the same exchange plan (b2_ep_plan_compute);
+//   1. route / scan the local tokens (moe_route_stage): per-expert counts on
+//      the device; the scatter of the rows into expert order (sorted_x) is
+//      launched next and runs while
+//   2. the [world][E] count matrix is all-gathered on the dispatch stream and
+//      copied to the host; one bounded host wait on it, then every rank
+//      computes the same exchange plan (b2_ep_plan_compute);
 //   3. dispatch: the copy engine pushes each peer's contiguous chunk of bf16
 //      rows straight into that peer's receive buffer (CUDA IPC mapping over
 //      NVLink), followed by a sequence-number flag -- no SMs are used;
@@ -85,6 +87,14 @@ const NcclApi &nccl() {
     }                                                                                  \
   } while (0)
 
+// Estimated grouped-GEMM cost beyond the rows themselves, in rows (balanced
+// plan): a row segment ends in a partly filled 256-row pair tile (128 rows
+// wasted on average), and every distinct expert a rank computes costs its
+// weight reads and tile-schedule ramp (~320 rows' time, from 2-GPU timelines
+// of skewed routing on B200).
+constexpr int64_t kEpSegmentCost = 128;
+constexpr int64_t kEpExpertCost = 320;
+
 // rows of source s (its expert-sorted order) whose global slot is < g
 int64_t rows_below(const int32_t *cnt_s, const int64_t *gpos_s, int E, int64_t g) {
   int64_t n = 0;
@@ -162,8 +172,52 @@ extern "C" b2_status b2_ep_plan_compute(int G, int r, int E, int mode, const int
     gstart += tot[e];
   }
   R = gstart;
+  // Rank boundaries split the estimated GEMM cost evenly: every row costs 1,
+  // every non-empty (expert, source) block of the global order kEpSegmentCost
+  // more (it becomes a row segment of the grouped GEMMs) and every expert
+  // kEpExpertCost more.  Splitting rows evenly instead leaves the rank with
+  // the many light experts of a skewed routing well behind the rank with the
+  // few heavy ones.  Each boundary stays within R/(4G) rows of the even row
+  // split, so every rank computes between 1/2 and 3/2 of the mean rows (the
+  // receive buffers hold 3/2).
+  int64_t C = R;
+  for (int e = 0; e < E; ++e) {
+    bool any = false;
+    for (int s = 0; s < G; ++s)
+      if (cnt[(size_t)s * E + e] > 0) {
+        C += kEpSegmentCost;
+        any = true;
+      }
+    if (any) C += kEpExpertCost;
+  }
   std::vector<int64_t> bound(G + 1);
-  for (int d = 0; d <= G; ++d) bound[d] = R * d / G;
+  bound[0] = 0;
+  bound[G] = R;
+  {
+    int d = 1;
+    int64_t row = 0, cost = 0;  // position and cost before the current block
+    for (int e = 0; e < E && d < G; ++e) {
+      bool first = true;
+      for (int s = 0; s < G && d < G; ++s) {
+        const int64_t c = cnt[(size_t)s * E + e];
+        if (c == 0) continue;
+        const int64_t ov = kEpSegmentCost + (first ? kEpExpertCost : 0);
+        first = false;
+        // boundaries whose target cost falls inside this block
+        while (d < G && C * d / G <= cost + ov + c) {
+          const int64_t over = C * d / G - cost - ov;
+          bound[d] = row + std::min<int64_t>(std::max<int64_t>(over, 0), c);
+          ++d;
+        }
+        row += c;
+        cost += ov + c;
+      }
+    }
+    for (; d < G; ++d) bound[d] = R;
+    const int64_t slack = R / (4 * G);
+    for (int q = 1; q < G; ++q)
+      bound[q] = std::min(std::max(bound[q], R * q / G - slack), R * q / G + slack);
+  }
   const int64_t *gpos_r = &gpos[(size_t)r * E];
   for (int d = 0; d < G; ++d) {
     const int64_t lo = rows_below(mine, gpos_r, E, bound[d]);
@@ -226,6 +280,7 @@ struct b2_ep {
   cudaStream_t st_d = nullptr, st_r = nullptr;  // copy-engine streams: dispatch / return
   std::vector<cudaEvent_t> ev_out;               // per exchange step
   cudaEvent_t ev_ready = nullptr, ev_ret = nullptr;
+  cudaEvent_t ev_scan = nullptr, ev_cnt = nullptr;  // counts ready / count matrix on the host
   int64_t cap_rows = 0;
   void *recv_x = nullptr, *inter = nullptr, *out_recv = nullptr;
   uint64_t *flags = nullptr;                     // [2][world]
@@ -239,6 +294,11 @@ struct b2_ep {
   int32_t *d_sched = nullptr, *h_sched = nullptr;  // per source: counts|offsets|mtile|group_b
   std::vector<b2_ep_plan> plans;                   // every rank's plan of the last forward
   double timeout_s = 60.0;
+  // timeline of the last forward while the layer's profiling is on
+  std::vector<cudaEvent_t> tl_ev;
+  std::vector<int> tl_tag;
+  int tl_n = 0;
+  double host_wait_ms = 0.0, host_enqueue_ms = 0.0;  // host side of the last forward
 };
 
 static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
@@ -288,11 +348,13 @@ static void ep_abort(b2_ep *ep) {
   ep->cm->ok = false;
 }
 
-// Wait for `s` with a bound; abort the communicator if a peer is lost.
-static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
+// Wait for `query` (a stream or an event) to report completion, with a
+// bound; abort the communicator if a peer is lost.
+template <typename Query>
+static b2_status bounded_wait(b2_ep *ep, Query query) {
   const auto t0 = std::chrono::steady_clock::now();
   while (true) {
-    const cudaError_t q = cudaStreamQuery(s);
+    const cudaError_t q = query();
     if (q == cudaSuccess) return B2_OK;
     if (q != cudaErrorNotReady) {
       fprintf(stderr, "[b2moe] stream error: %s\n", cudaGetErrorString(q));
@@ -311,8 +373,16 @@ static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
       ep_abort(ep);
       return B2_ERR_COMM;
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    // The per-forward wait (count all-gather) normally ends within tens of
+    // microseconds and the GPU may idle until it does: poll without sleeping
+    // for the first milliseconds (a 20 us sleep costs 60-80 us with the
+    // kernel's timer slack), then back off.
+    if (el > 5e-3) std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
+}
+
+static b2_status bounded_sync(b2_ep *ep, cudaStream_t s) {
+  return bounded_wait(ep, [s] { return cudaStreamQuery(s); });
 }
 
 extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
@@ -344,6 +414,9 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   for (cudaEvent_t e : ep->ev_out) cudaEventDestroy(e);
   if (ep->ev_ready) cudaEventDestroy(ep->ev_ready);
   if (ep->ev_ret) cudaEventDestroy(ep->ev_ret);
+  if (ep->ev_scan) cudaEventDestroy(ep->ev_scan);
+  for (cudaEvent_t e : ep->tl_ev) cudaEventDestroy(e);
+  if (ep->ev_cnt) cudaEventDestroy(ep->ev_cnt);
   if (ep->st_d) cudaStreamDestroy(ep->st_d);
   if (ep->st_r) cudaStreamDestroy(ep->st_r);
   if (ep->h_cnt_all) cudaFreeHost(ep->h_cnt_all);
@@ -388,7 +461,8 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
   const int64_t local_rows = (int64_t)desc->max_tokens * desc->top_k;
   // receive-side rows; the inter buffer also holds the rank's own rows, which
   // are computed in place at their expert-sorted positions
-  ep->cap_rows = mode == B2_EP_OWNER ? local_rows * world : local_rows + world;
+  ep->cap_rows =
+      mode == B2_EP_OWNER ? local_rows * world : local_rows + local_rows / 2 + world + 1;
   const int64_t inter_rows = std::max<int64_t>(ep->cap_rows, local_rows);
   auto fail = [&](b2_status s) {
     b2_ep_destroy(ep);
@@ -422,7 +496,9 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
   if (cudaStreamCreateWithFlags(&ep->st_d, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ep->st_r, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->ev_ready, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->ev_ret, cudaEventDisableTiming) != cudaSuccess)
+      cudaEventCreateWithFlags(&ep->ev_ret, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_scan, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_cnt, cudaEventDisableTiming) != cudaSuccess)
     return fail(B2_ERR_CUDA);
   ep->ev_out.resize(world, nullptr);
   for (int k = 0; k < world; ++k)
@@ -537,22 +613,49 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   const int E = ep->E, G = ep->world, r = ep->rank, H = m->d.hidden;
   const size_t rb = (m->tf32 ? 4 : 2) * (size_t)H;  // bytes per row
   const uint64_t timeout_ns = (uint64_t)(ep->timeout_s * 1e9);
+  auto tl = [&](int tag) -> b2_status {
+    if (!m->profile) return B2_OK;
+    if (ep->tl_n >= (int)ep->tl_ev.size()) {
+      cudaEvent_t e = nullptr;
+      B2_CUDA(cudaEventCreate(&e));
+      ep->tl_ev.push_back(e);
+      ep->tl_tag.push_back(0);
+    }
+    ep->tl_tag[ep->tl_n] = tag;
+    B2_CUDA(cudaEventRecord(ep->tl_ev[ep->tl_n++], s));
+    return B2_OK;
+  };
+  ep->tl_n = 0;
+  B2_RETURN_IF(tl(B2_EP_TL_START));
 
-  // 1. local routing (also for T == 0: the rank still takes part in the exchange)
+  // 1. local routing and scan (also for T == 0: the rank still takes part in
+  // the exchange)
   if (T > 0) {
-    B2_RETURN_IF(moe_route_stage(m, x, T, nullptr, s));
+    B2_RETURN_IF(moe_route_stage(m, x, T, nullptr, s, false));
   } else {
     for (int i = 0; i < 3; ++i) prof_mark(m, s);  // keep the stage-event layout
     B2_CUDA(cudaMemsetAsync(m->counts, 0, sizeof(int) * E, s));
   }
-  prof_mark(m, s);  // exchange + expert GEMMs start
-  // 2. count matrix -> host.  The all-gather completes only after every rank's
-  // previous forward finished on its stream, so after this point every peer
-  // buffer written below is free for this forward.
-  B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->cm->comm, s));
+  // 2. count matrix -> host on the dispatch stream while `s` runs the scatter,
+  // so the host round trip hides behind it.  The all-gather starts after this
+  // rank's scan, which follows its previous forward on `s`; so once it has
+  // completed, every rank's previous forward is done and every peer buffer
+  // written below is free for this forward.
+  B2_CUDA(cudaEventRecord(ep->ev_scan, s));
+  B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_scan, 0));
+  B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->cm->comm, ep->st_d));
   B2_CUDA(cudaMemcpyAsync(ep->h_cnt_all, ep->d_cnt_all, sizeof(int32_t) * G * E,
-                          cudaMemcpyDeviceToHost, s));
-  B2_RETURN_IF(bounded_sync(ep, s));
+                          cudaMemcpyDeviceToHost, ep->st_d));
+  B2_CUDA(cudaEventRecord(ep->ev_cnt, ep->st_d));
+  if (T > 0) B2_RETURN_IF(moe_scatter_stage(m, x, T, s));
+  prof_mark(m, s);  // exchange + expert GEMMs start
+  B2_RETURN_IF(tl(B2_EP_TL_SCATTERED));
+  const auto h0 = std::chrono::steady_clock::now();
+  {
+    cudaEvent_t ev = ep->ev_cnt;
+    B2_RETURN_IF(bounded_wait(ep, [ev] { return cudaEventQuery(ev); }));
+  }
+  const auto h1 = std::chrono::steady_clock::now();
   for (int q = 0; q < G; ++q)
     B2_RETURN_IF(b2_ep_plan_compute(G, q, E, ep->mode, ep->h_cnt_all, &ep->plans[q]));
   const b2_ep_plan &p = ep->plans[r];
@@ -582,6 +685,7 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   B2_CUDA(cudaMemcpyAsync(ep->d_wait_idx, ep->h_wait_idx, sizeof(int) * 2 * G,
                           cudaMemcpyHostToDevice, s));
   B2_CUDA(cudaEventRecord(ep->ev_ready, s));
+  B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
 
   auto sched_of = [&](int src) {
     GemmSched sc;
@@ -612,6 +716,7 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   if (nseg[r] > 0)
     B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(r), s,
                                 false));
+  B2_RETURN_IF(tl(B2_EP_TL_OWN_FIRST));
   // 5. per step: wait for the rows of rank r-k, expert GEMMs, return them
   const char *ro = reinterpret_cast<const char *>(ep->out_recv);
   for (int k = 1; k < G; ++k) {
@@ -620,8 +725,10 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
       wait_flags_kernel<<<1, 32, 0, s>>>(ep->flags, ep->d_wait_idx + from, 1, ep->seq, timeout_ns,
                                          m->status);
       B2_LAUNCHED();
+      B2_RETURN_IF(tl(B2_EP_TL_ARRIVED));
       B2_RETURN_IF(moe_gemm_stage(m, ep->tm_recv, ep->tm_inter, ep->inter, ep->out_recv,
                                   sched_of(from), s, false));
+      B2_RETURN_IF(tl(B2_EP_TL_REMOTE_DONE));
     }
     B2_CUDA(cudaEventRecord(ep->ev_out[k], s));
     B2_CUDA(cudaStreamWaitEvent(ep->st_r, ep->ev_out[k], 0));
@@ -636,6 +743,7 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   if (nseg[G] > 0)
     B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(G), s,
                                 false));
+  B2_RETURN_IF(tl(B2_EP_TL_OWN_SECOND));
   prof_mark(m, s);  // expert GEMMs done; waiting for returns
   if (nwait_ret > 0) {
     wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(
@@ -647,18 +755,41 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
     B2_CUDA(cudaEventRecord(ep->ev_ret, ep->st_r));
     B2_CUDA(cudaStreamWaitEvent(s, ep->ev_ret, 0));
   }
+  B2_RETURN_IF(tl(B2_EP_TL_RETURNED));
   // 6. local k-ordered combine
   if (T > 0) {
     B2_RETURN_IF(moe_combine_stage(m, y, T, s, accumulate));
   } else {
     for (int i = 0; i < 2; ++i) prof_mark(m, s);
   }
-  return B2_OK;
+  ep->host_wait_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+  ep->host_enqueue_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - h1).count();
+  return tl(B2_EP_TL_DONE);
 }
 
 extern "C" b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int T,
                                    b2_stream stream) {
   return ep_forward_impl(ep, x, y, T, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" b2_status b2_ep_profile_timeline(b2_ep *ep, int max, int *tags, float *ms, int *n) {
+  if (!ep || max < 0 || !n || (max > 0 && (!tags || !ms))) return B2_ERR_INVALID;
+  int k = std::min(max, ep->tl_n);
+  if (ep->tl_n > 0) B2_CUDA(cudaEventSynchronize(ep->tl_ev[ep->tl_n - 1]));
+  for (int i = 0; i < k; ++i) {
+    tags[i] = ep->tl_tag[i];
+    ms[i] = 0.0f;
+    if (i > 0) B2_CUDA(cudaEventElapsedTime(&ms[i], ep->tl_ev[0], ep->tl_ev[i]));
+  }
+  if (ep->tl_n > 0 && k + 2 <= max) {
+    tags[k] = B2_EP_TL_HOST_WAIT;
+    ms[k++] = (float)ep->host_wait_ms;
+    tags[k] = B2_EP_TL_HOST_ENQUEUE;
+    ms[k++] = (float)ep->host_enqueue_ms;
+  }
+  *n = k;
+  return B2_OK;
 }
 
 extern "C" b2_status b2_ep_set_timeout(b2_ep *ep, double seconds) {

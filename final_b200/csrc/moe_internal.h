@@ -331,9 +331,12 @@ b2_status moe_create_impl(const b2_moe_desc *desc, int n_wexp, const float *cons
 b2_status moe_alloc(b2_moe *m, void **p, size_t bytes);
 void prof_mark(b2_moe *m, cudaStream_t s);
 
-// route + scan + scatter of T local tokens into m->sorted_x (expert order)
+// route + scan (+ scatter unless with_scatter is false) of T local tokens;
+// after the scan m->counts holds the per-expert row counts
 b2_status moe_route_stage(b2_moe *m, const float *x, int T, const b2_moe_trace *tr,
-                          cudaStream_t s);
+                          cudaStream_t s, bool with_scatter = true);
+// scatter of the routed tokens into m->sorted_x (expert order)
+b2_status moe_scatter_stage(b2_moe *m, const float *x, int T, cudaStream_t s);
 // W1||W3 + SwiGLU and W2 over the scheduled row segments of A (rows of tm_a1)
 b2_status moe_gemm_stage(b2_moe *m, const CUtensorMap &tm_a1, const CUtensorMap &tm_a2,
                          void *inter, void *out, const GemmSched &sched, cudaStream_t s,

@@ -25,21 +25,27 @@ constexpr int kMaxExperts = 32;
 constexpr int kMaxTopK = 8;
 
 // ---------------------------------------------------------------------------
-// route_kernel: one warp per 32 tokens.
+// route_kernel: one block of two warps per 32 tokens, 16 tokens per warp.
 // logits[t,e] = fold_k fma(x[t,k], gate[e,k], acc) from 0.0f -- the order of
 // attn_matmul_tiled_kernel (src/layer.cu:70-130), so logits are bit-exact.
+// Every dot product is one sequential chain, so the only parallelism is
+// (token, expert) pairs: at 16k tokens that is 16k lanes of 32 accumulators or
+// 32k lanes of 16.  The narrower split gives every SM sub-partition two warps
+// to interleave (one warp alone waits on its own shared-memory and cp.async
+// latencies) and 2x the blocks to even out the last wave.
 //
 // x and gateT (= gate^T, [H][32]) stream through a kRouteStages-deep cp.async
-// ring of 32-wide k-chunks: xs[t][k] holds 32 tokens x 32 k fp32 in rows
-// padded to 36 floats (the 4 rows one 128-bit load touches fall in distinct
-// bank groups, and every load offset is a compile-time constant); gs[k][e] is
-// the gate chunk.  A block is one warp, so the ring needs only warp-level
-// synchronisation.  Lane (tg = lane%4, eg = lane/4) owns tokens tg+4i (i<8)
-// x experts 4eg..4eg+3 (32 accumulators): per 4 k-steps, 12 128-bit shared
-// loads feed 128 FFMAs, each accumulator updated in strict k order.
+// ring of 32-wide k-chunks shared by the block: xs[t][k] holds 32 tokens x
+// 32 k fp32 in rows padded to 36 floats (the 4 rows one 128-bit load touches
+// fall in distinct bank groups, and every load offset is a compile-time
+// constant); gs[k][e] is the gate chunk, read by both warps.  One 64-thread
+// barrier per chunk.  Lane (tg = lane%4, eg = lane/4) of warp w owns tokens
+// 16w+tg+4i (i<4) x experts 4eg..4eg+3 (16 accumulators): per 4 k-steps,
+// 8 128-bit shared loads (broadcasts: one wavefront each) feed 64 FFMAs, each
+// accumulator updated in strict k order.
 // ---------------------------------------------------------------------------
 constexpr int kRouteStages = 4;
-constexpr int kRouteThreads = 32;
+constexpr int kRouteThreads = 64;
 constexpr int kRouteXRow = kRouteKC + 4;  // padded row (floats)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
@@ -66,20 +72,21 @@ static __global__ void __launch_bounds__(kRouteThreads)
   __shared__ float lg[kRouteTB][kMaxExperts + 1];
   __shared__ int hist[kMaxExperts];
 
-  const int lane = threadIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, w = tid >> 5;
   const int t0 = blockIdx.x * kRouteTB;
   const int NC = H / kRouteKC;
-  hist[lane] = 0;
+  if (tid < kMaxExperts) hist[tid] = 0;
   pdl_wait();
   pdl_trigger();
 
-  // chunk kc -> stage st: 8 x 16 B of x and 8 x 16 B of the gate per lane;
-  // rows past T are zero-filled (src-size 0)
+  // chunk kc -> stage st: per thread 4 x 16 B of x (rows of its own warp) and
+  // 4 x 16 B of the gate; rows past T are zero-filled (src-size 0)
   auto issue = [&](int kc, int st) {
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const int idx = lane + 32 * m;  // 0..255
-      const int row = idx >> 3, c = idx & 7;
+    for (int m = 0; m < 4; ++m) {
+      const int idx = lane + 32 * m;  // 0..127 within the warp's 16 rows
+      const int row = 16 * w + (idx >> 3), c = idx & 7;
       const int t = t0 + row;
       const bool ok = t < T;
       const float *src = x + (size_t)(ok ? t : 0) * H + kc * kRouteKC + c * 4;
@@ -87,16 +94,16 @@ static __global__ void __launch_bounds__(kRouteThreads)
     }
     const float *gsrc = gateT + (size_t)kc * kRouteKC * kMaxExperts;
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const int idx = lane + 32 * m;  // 0..255
+    for (int m = 0; m < 4; ++m) {
+      const int idx = tid + kRouteThreads * m;  // 0..255
       cp_async16(smem_u32(&gs[st][idx * 4]), gsrc + idx * 4, 16u);
     }
   };
 
   const int tg = lane & 3, eg = lane >> 2;
-  float acc[8][4];
+  float acc[4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
 
@@ -107,17 +114,19 @@ static __global__ void __launch_bounds__(kRouteThreads)
   }
   for (int kc = 0; kc < NC; ++kc) {
     cp_async_wait<kRouteStages - 2>();
-    __syncwarp();
+    // chunk kc has landed for every thread, and every thread is done with
+    // chunk kc-1, whose stage the next issue refills
+    __syncthreads();
     const int nk = kc + kRouteStages - 1;
     if (nk < NC) issue(nk, nk % kRouteStages);
     cp_async_commit();
-    const float *xb = xs[kc % kRouteStages] + tg * kRouteXRow;
+    const float *xb = xs[kc % kRouteStages] + (16 * w + tg) * kRouteXRow;
     const float *gb = gs[kc % kRouteStages] + eg * 4;
-#pragma unroll 2
+#pragma unroll 4
     for (int q = 0; q < kRouteKC / 4; ++q) {  // k-quad q: k = 4q .. 4q+3
-      float4 xv[8], gv[4];
+      float4 xv[4], gv[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 4; ++i)
         xv[i] = *reinterpret_cast<const float4 *>(xb + 4 * i * kRouteXRow + 4 * q);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -126,21 +135,20 @@ static __global__ void __launch_bounds__(kRouteThreads)
       for (int j = 0; j < 4; ++j) {
         const float ge[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const float xk = j == 0 ? xv[i].x : j == 1 ? xv[i].y : j == 2 ? xv[i].z : xv[i].w;
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[i][e] = __fmaf_rn(xk, ge[e], acc[i][e]);
         }
       }
     }
-    __syncwarp();  // every lane is done with this stage before it is refilled
   }
   cp_async_wait<0>();
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) lg[tg + 4 * i][eg * 4 + e] = acc[i][e];
-  __syncwarp();
+    for (int e = 0; e < 4; ++e) lg[16 * w + tg + 4 * i][eg * 4 + e] = acc[i][e];
+  __syncthreads();
 
   if (threadIdx.x < kRouteTB) {
     const int tl = threadIdx.x;

@@ -7,8 +7,10 @@ include/b2moe_ep.h; torch.distributed is only used here to hand the NCCL
 unique id from rank 0 to the others.
 
 Placement (``mode``): "owner" -- rank r holds experts [r*E/G, (r+1)*E/G);
-"balanced" -- every rank holds all experts and computes an equal share of the
-expert-sorted rows (skew-proof).
+"balanced" -- every rank holds all experts and computes a contiguous share of
+the globally expert-sorted rows; the shares split the estimated GEMM cost
+(rows + 128 per non-empty (expert, source) block + 320 per expert) evenly
+(skew-proof).
 """
 from __future__ import annotations
 
@@ -119,6 +121,17 @@ class ExpertParallelMoE:
         check(self.lib.b2_moe_profile_read(self._layer(), ms, C.byref(n)), "profile_read")
         from .moe import SparseMoeBlock
         return dict(zip(SparseMoeBlock.STAGES, list(ms))), n.value
+
+    TIMELINE = ("start", "scattered", "planned", "own_first", "arrived", "remote_done",
+                "own_second", "returned", "done", "host_wait", "host_enqueue")
+
+    def timeline(self) -> list:
+        """[(mark, us since the forward started)] of the last forward run with
+        profiling on (b2_ep_profile_timeline)."""
+        tags, ms, n = (C.c_int * 64)(), (C.c_float * 64)(), C.c_int(0)
+        check(self.lib.b2_ep_profile_timeline(self._h, 64, tags, ms, C.byref(n)),
+              "b2_ep_profile_timeline")
+        return [(self.TIMELINE[tags[i]], round(ms[i] * 1e3, 1)) for i in range(n.value)]
 
     def device_status(self) -> int:
         v = C.c_int(0)

@@ -162,7 +162,7 @@ b2_status b2_lfm2_create(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,
  * caller).  Collective: create, every forward and destroy are called by all
  * ranks in the same order; a rank with no tokens calls b2_lfm2_forward with
  * batch 0 and still takes part in every layer's exchange.  Each forward
- * synchronises `stream` once per MoE layer (the count all-gather of
+ * waits on the host once per MoE layer (the count all-gather of
  * b2_ep_forward); logits are bit-identical to b2_lfm2_create's model on the
  * same tokens. */
 b2_status b2_lfm2_create_ep(const b2_lfm2_desc *desc, b2_weight_fn get, void *ctx,

@@ -15,9 +15,14 @@
  *   B2_EP_OWNER     rank r holds experts [r*E/G, (r+1)*E/G) (E divisible by G)
  *                   and computes every row routed to them;
  *   B2_EP_BALANCED  every rank holds all E experts' weights (705 MB in bf16 for
- *                   the reference model) and computes an equal contiguous share
- *                   of the globally expert-sorted rows, which removes the load
- *                   imbalance of skewed (e.g. Zipf) routing.
+ *                   the reference model) and computes a contiguous share of
+ *                   the globally expert-sorted rows (expert-major, then source
+ *                   rank), which removes the load imbalance of skewed (e.g.
+ *                   Zipf) routing.  Shares split the estimated GEMM cost
+ *                   evenly: rows, plus 128 rows' worth per non-empty (expert,
+ *                   source) block (a row segment with a partly filled tile)
+ *                   and 320 per expert (its weight reads); each rank keeps
+ *                   between 1/2 and 3/2 of the mean rows.
  * Both produce bit-identical y to the single-GPU b2_moe_forward on the same
  * tokens: every row goes through the same kernels in the same order.
  */
@@ -73,8 +78,9 @@ b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
                        const float *gate, const float *bias, int weights_on_host,
                        b2_stream stream, b2_ep **out);
 
-/* Collective.  y[T,H] = MoE(x[T,H]) for this rank's T tokens.  Synchronises
- * `stream` once to size the exchange (the count all-gather); returns
+/* Collective.  y[T,H] = MoE(x[T,H]) for this rank's T tokens.  Waits on the
+ * host once to size the exchange (the count all-gather, which runs beside the
+ * scatter of the rows into expert order); returns
  * B2_ERR_COMM if a peer does not answer within the timeout (the communicator
  * is then aborted).  Rows for rank r+k are pushed by the copy engine into that
  * rank's receive buffer followed by a sequence-number flag; each rank runs its
@@ -96,6 +102,29 @@ b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int num_tokens,
 b2_status b2_flag_wait(const uint64_t *flags, const int *idx, int n,
                        uint64_t target, double timeout_s, int *status,
                        b2_stream stream);
+
+/* Marks of the expert-parallel forward's timeline, in stream order. */
+enum {
+  B2_EP_TL_START = 0,       /* forward entered (before routing) */
+  B2_EP_TL_SCATTERED = 1,   /* rows scattered into expert order */
+  B2_EP_TL_PLANNED = 2,     /* count matrix on the host, plan made, schedules uploaded */
+  B2_EP_TL_OWN_FIRST = 3,   /* first part of the rank's own rows through both GEMMs */
+  B2_EP_TL_ARRIVED = 4,     /* one source's rows have arrived (after its flag wait) */
+  B2_EP_TL_REMOTE_DONE = 5, /* that source's rows through both GEMMs */
+  B2_EP_TL_OWN_SECOND = 6,  /* second part of the own rows through both GEMMs */
+  B2_EP_TL_RETURNED = 7,    /* every peer has returned this rank's results */
+  B2_EP_TL_DONE = 8,        /* combine done */
+  /* host-side durations of the same forward (ms, not times since the first mark) */
+  B2_EP_TL_HOST_WAIT = 9,   /* the host's wait for the count matrix */
+  B2_EP_TL_HOST_ENQUEUE = 10 /* from that wait's end until the forward returned */
+};
+
+/* Timeline of the last forward run with profiling on (b2_moe_profile_enable
+ * on b2_ep_layer(ep)): *n marks (at most max), tags[i] one of B2_EP_TL_*,
+ * ms[i] the device time from the first mark (CUDA events on the forward's
+ * stream), followed by the two host durations.  Waits for the last mark.  No
+ * counterpart in the reference. */
+b2_status b2_ep_profile_timeline(b2_ep *ep, int max, int *tags, float *ms, int *n);
 
 /* Host-side bound (seconds) on every wait for the peers (default 60). */
 b2_status b2_ep_set_timeout(b2_ep *ep, double seconds);

@@ -12,6 +12,41 @@ import pytest
 from final_b200 import ep as epmod
 
 
+SEG_COST, EXPERT_COST = 128, 320  # estimated GEMM cost beyond the rows, in rows
+
+
+def _balanced_rows(cnt):
+    """Rows each rank computes under the balanced plan, restated: the
+    boundaries split rows + SEG_COST per non-empty (expert, source) block +
+    EXPERT_COST per expert of the global order (expert-major, then source)
+    evenly, each clamped to within R/(4G) of the even row split."""
+    G, E = cnt.shape
+    R = int(cnt.sum())
+    C = R + SEG_COST * int((cnt > 0).sum()) + EXPERT_COST * int((cnt.sum(0) > 0).sum())
+    bound = [0] * (G + 1)
+    bound[G] = R
+    d, row, cost = 1, 0, 0
+    for e in range(E):
+        first = True
+        for s in range(G):
+            c = int(cnt[s, e])
+            if c == 0 or d >= G:
+                continue
+            ov = SEG_COST + (EXPERT_COST if first else 0)
+            first = False
+            while d < G and C * d // G <= cost + ov + c:
+                bound[d] = row + min(max(C * d // G - cost - ov, 0), c)
+                d += 1
+            row += c
+            cost += ov + c
+    for q in range(d, G):
+        bound[q] = R
+    slack = R // (4 * G)
+    for q in range(1, G):
+        bound[q] = min(max(bound[q], R * q // G - slack), R * q // G + slack)
+    return [bound[q + 1] - bound[q] for q in range(G)]
+
+
 def _random_counts(rng, world, E, zipf=False):
     if zipf:
         p = np.arange(1, E + 1) ** -1.1
@@ -48,8 +83,11 @@ def test_plan_invariants(mode, world, zipf):
                 cover[o:o + c] += 1
                 assert 0 <= e < (E // world if mode == "owner" else E)
             assert np.all(cover == 1)
-            if mode == "balanced":
-                assert abs(p["recv_rows"] - R / world) <= 1
+        if mode == "balanced":
+            rows = [p["recv_rows"] for p in plans]
+            assert rows == _balanced_rows(cnt)
+            for n in rows:
+                assert R / world * 0.5 - 2 <= n <= R / world * 1.5 + 2
 
 
 def test_plan_balanced_removes_zipf_skew():
@@ -59,9 +97,14 @@ def test_plan_balanced_removes_zipf_skew():
     p /= p.sum()
     cnt = np.stack([rng.multinomial(16384 * 4, p) for _ in range(world)]).astype(np.int32)
     own = [epmod.plan(cnt, r, "owner")["recv_rows"] for r in range(world)]
-    bal = [epmod.plan(cnt, r, "balanced")["recv_rows"] for r in range(world)]
+    plans = [epmod.plan(cnt, r, "balanced") for r in range(world)]
     assert max(own) / np.mean(own) > 2.5          # hot experts pile onto rank 0
-    assert max(bal) / np.mean(bal) < 1.0001
+    # estimated cost per rank: rows + SEG_COST per segment + EXPERT_COST per expert
+    cost = [p["recv_rows"] + SEG_COST * len(p["seg_cnt"]) + EXPERT_COST * len(set(p["seg_expert"]))
+            for p in plans]
+    assert max(cost) / np.mean(cost) < 1.03
+    rows = [p["recv_rows"] for p in plans]
+    assert max(rows) / np.mean(rows) <= 1.5
 
 
 def test_plan_rejects_bad_input():
