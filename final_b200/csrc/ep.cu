@@ -304,9 +304,14 @@ struct b2_ep {
 static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
 
 // Bounded wait, on this GPU, for flags[idx[i]] >= target (one lane per flag).
-// Gives up after timeout_ns, recording kDevTimeoutPeer in *status.
+// Gives up after timeout_ns, recording kDevTimeoutPeer in *status.  Launched
+// with programmatic dependent launch between two GEMM stages, it lets the next
+// stage's GEMM launch (and run its prologue) at once, and completes only after
+// the flags and its predecessor in the stream: the GEMM's griddepcontrol.wait
+// therefore orders it after both.
 static __global__ void wait_flags_kernel(const volatile uint64_t *flags, const int *idx, int n,
                                          uint64_t target, uint64_t timeout_ns, int *status) {
+  pdl_trigger();
   const int i = threadIdx.x;
   if (i < n) {
     const uint64_t t0 = globaltimer();
@@ -319,6 +324,7 @@ static __global__ void wait_flags_kernel(const volatile uint64_t *flags, const i
     }
   }
   __threadfence_system();
+  pdl_wait();
 }
 
 extern "C" b2_status b2_flag_wait(const uint64_t *flags, const int *idx, int n, uint64_t target,
@@ -722,9 +728,10 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   for (int k = 1; k < G; ++k) {
     const int from = (r - k + G) % G;
     if (p.recv_cnt[from] > 0) {
-      wait_flags_kernel<<<1, 32, 0, s>>>(ep->flags, ep->d_wait_idx + from, 1, ep->seq, timeout_ns,
-                                         m->status);
-      B2_LAUNCHED();
+      B2_RETURN_IF(launch_pdl(wait_flags_kernel, dim3(1), dim3(32), 0, s,
+                              (const volatile uint64_t *)ep->flags,
+                              (const int *)(ep->d_wait_idx + from), 1, ep->seq, timeout_ns,
+                              m->status));
       B2_RETURN_IF(tl(B2_EP_TL_ARRIVED));
       B2_RETURN_IF(moe_gemm_stage(m, ep->tm_recv, ep->tm_inter, ep->inter, ep->out_recv,
                                   sched_of(from), s, false));
