@@ -501,6 +501,36 @@ LFM2Model::LFM2Model(const std::string &model_file) : loader_(model_file) {
   cuda_check(cudaSetDevice(0), "cudaSetDevice");
 }
 
+LFM2Model::LFM2Model(const std::string &model_file, int world, int rank,
+                     const std::string &unique_id, bool owner_placement)
+    : loader_(model_file) {
+  desc_ = infer_desc(loader_);
+  if (unique_id.size() != B2_EP_UNIQUE_ID_BYTES) die("LFM2Model", "unique id of the wrong size");
+  int n = 0;
+  cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (n < 1) die("LFM2Model", "no CUDA device");
+  replicas_.resize(1);
+  Replica &r = replicas_[0];
+  r.device = rank % n;
+  cuda_check(cudaSetDevice(r.device), "cudaSetDevice");
+  cuda_check(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(b2_lfm2_create_ep(&desc_, b2_loader_weight, loader_.handle(), /*weights_on_host=*/1,
+                          world, rank, unique_id.data(),
+                          owner_placement ? B2_EP_OWNER : B2_EP_BALANCED,
+                          reinterpret_cast<b2_stream>(r.stream), &r.model),
+        "b2_lfm2_create_ep");
+  cuda_check(cudaMalloc(&r.ids, (size_t)desc_.max_batch * desc_.max_seq * sizeof(int)),
+             "cudaMalloc");
+  cuda_check(cudaMalloc(&r.logits, (size_t)desc_.max_batch * desc_.vocab * sizeof(float)),
+             "cudaMalloc");
+}
+
+std::string LFM2Model::unique_id() {
+  std::string id(B2_EP_UNIQUE_ID_BYTES, '\0');
+  check(b2_ep_unique_id(&id[0]), "b2_ep_unique_id");
+  return id;
+}
+
 LFM2Model::~LFM2Model() {
   for (Replica &r : replicas_) {
     cudaSetDevice(r.device);

@@ -271,6 +271,18 @@ void set_model_limits(int max_batch, int max_seq);
 class LFM2Model {
  public:
   explicit LFM2Model(const std::string &model_file);
+  // The expert-parallel model, one process per GPU (b2_lfm2_create_ep): this
+  // process is `rank` of `world` and uses device rank % (visible devices);
+  // every MoE layer exchanges expert rows with the other ranks over NVLink
+  // instead of the reference's stages passing the whole residual stream.
+  // unique_id is LFM2Model::unique_id() of rank 0, shared by the caller (MPI,
+  // a file, ...).  Construction, forward(), sync() and destruction are
+  // collective: every rank calls them in the same order, each forward() with
+  // its own batch.  Logits are bit-identical to the single-GPU model's.
+  LFM2Model(const std::string &model_file, int world, int rank, const std::string &unique_id,
+            bool owner_placement = false);
+  // A fresh NCCL unique id (B2_EP_UNIQUE_ID_BYTES bytes) for the constructor above.
+  static std::string unique_id();
   ~LFM2Model();
   LFM2Model(const LFM2Model &) = delete;
   LFM2Model &operator=(const LFM2Model &) = delete;

@@ -10,6 +10,11 @@
 //   b2_layers_run conv    <weights> <layer> <batch> <seq> <x.f32> <y.f32>
 //   b2_layers_run decoder <weights> <layer> <is_attention> <batch> <seq> <x.f32> <y.f32>
 //   b2_layers_run model   <model.bin> <batch> <seq> <ids.i32> <logits.f32>
+//   b2_layers_run model_ep <model.bin> <batch> <seq> <ids.i32> <logits.f32>
+//                          <world> <rank> <id file> [balanced|owner]
+//
+// model_ep is one rank of the expert-parallel model: rank 0 writes the NCCL
+// unique id to <id file>, the other ranks wait for it (60 s at most).
 //
 // <weights> is a directory of <name>.f32 / <name>.shape files or a model file
 // in the reference's format.  x is [tokens][hidden] fp32; y the same.
@@ -18,6 +23,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <ctime>
 #include <fstream>
 #include <memory>
 #include <string>
@@ -42,7 +48,9 @@ static void usage() {
           "       b2_layers_run attn|conv <weights> <layer> <batch> <seq> <x.f32> <y.f32>\n"
           "       b2_layers_run decoder <weights> <layer> <is_attention> <batch> <seq> <x.f32> "
           "<y.f32>\n"
-          "       b2_layers_run model <model.bin> <batch> <seq> <ids.i32> <logits.f32>\n");
+          "       b2_layers_run model <model.bin> <batch> <seq> <ids.i32> <logits.f32>\n"
+          "       b2_layers_run model_ep <model.bin> <batch> <seq> <ids.i32> <logits.f32> "
+          "<world> <rank> <id file> [balanced|owner]\n");
 }
 
 template <typename T>
@@ -91,6 +99,65 @@ static int run_model(int argc, char **argv) {
   return 0;
 }
 
+// Rank 0 publishes the id (write, then rename: readers never see half a
+// file); the others poll for it.
+static bool share_unique_id(const std::string &path, int rank, std::string *id) {
+  if (rank == 0) {
+    *id = b2layer::LFM2Model::unique_id();
+    const std::string tmp = path + ".tmp";
+    {
+      std::ofstream f(tmp, std::ios::binary);
+      f.write(id->data(), (std::streamsize)id->size());
+      if (!f) return false;
+    }
+    return rename(tmp.c_str(), path.c_str()) == 0;
+  }
+  for (int i = 0; i < 6000; ++i) {
+    std::ifstream f(path, std::ios::binary);
+    if (f) {
+      id->assign(B2_EP_UNIQUE_ID_BYTES, '\0');
+      f.read(&(*id)[0], B2_EP_UNIQUE_ID_BYTES);
+      if (f.gcount() == B2_EP_UNIQUE_ID_BYTES) return true;
+    }
+    struct timespec ts = {0, 10 * 1000 * 1000};
+    nanosleep(&ts, nullptr);
+  }
+  return false;
+}
+
+static int run_model_ep(int argc, char **argv) {
+  if (argc < 10) {
+    usage();
+    return 2;
+  }
+  const int B = atoi(argv[3]), S = atoi(argv[4]);
+  const int world = atoi(argv[7]), rank = atoi(argv[8]);
+  const bool owner = argc > 10 && !strcmp(argv[10], "owner");
+  std::string id;
+  if (!share_unique_id(argv[9], rank, &id)) {
+    fprintf(stderr, "rank %d: no unique id in %s\n", rank, argv[9]);
+    return 1;
+  }
+  b2layer::set_model_limits(B, S);
+  b2layer::LFM2Model model(argv[2], world, rank, id, owner);
+  std::vector<int> ids((size_t)B * S);
+  if (!read_file(argv[5], &ids)) {
+    fprintf(stderr, "short read of %s\n", argv[5]);
+    return 1;
+  }
+  std::vector<float> logits((size_t)B * model.vocab()), again(logits.size());
+  model.forward(0, B, ids.data(), S, logits.data());
+  model.forward(B, B, ids.data(), S, again.data());
+  model.sync();
+  if (memcmp(logits.data(), again.data(), logits.size() * sizeof(float)) != 0) {
+    fprintf(stderr, "two forwards of the same ids differ\n");
+    return 1;
+  }
+  write_file(argv[6], logits);
+  printf("ok model_ep rank %d of %d B=%d S=%d V=%d\n", rank, world, B, S, model.vocab());
+  return 0;
+}
+
 int main(int argc, char **argv) {
   if (argc == 2 && (!strcmp(argv[1], "--help") || !strcmp(argv[1], "-h"))) {
     usage();
@@ -102,6 +169,7 @@ int main(int argc, char **argv) {
   }
   const std::string kind = argv[1];
   if (kind == "model") return run_model(argc, argv);
+  if (kind == "model_ep") return run_model_ep(argc, argv);
   const bool seq_form = kind == "attn" || kind == "conv" || kind == "decoder";
   const int need = kind == "decoder" ? 9 : seq_form ? 8 : 7;
   if (argc < need) {

@@ -160,3 +160,65 @@ def test_cpp_model_from_file(cuda_dev, tiny_file, tmp_path):
     want = lc.model_oracle(W, ids, cfg["layers"])
     print(f"C++ LFM2Model logits vs oracle: {_rel(logits, want):.2e}")
     assert _rel(logits, want) < 5e-3  # measured 5.5e-4 on a B200
+
+
+def _cpp_model_logits(p, ids, B, S, V, out):
+    idf = out.with_suffix(".i32")
+    idf.write_bytes(ids.astype(np.int32).tobytes())
+    r = subprocess.run([str(RUN), "model", str(p), str(B), str(S), str(idf), str(out)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return np.frombuffer(out.read_bytes(), dtype=np.float32).reshape(B, V)
+
+
+def _cpp_model_ep(p, ids_list, B, S, V, tmp_path, placement):
+    """Start one model_ep rank per entry of ids_list; returns their logits."""
+    world = len(ids_list)
+    idfile = tmp_path / f"uid_{placement}_{world}"
+    procs, outs = [], []
+    for rank, ids in enumerate(ids_list):
+        idf, lf = tmp_path / f"ep_ids{rank}.i32", tmp_path / f"ep_logits{rank}.f32"
+        idf.write_bytes(ids.astype(np.int32).tobytes())
+        outs.append(lf)
+        procs.append(subprocess.Popen(
+            [str(RUN), "model_ep", str(p), str(B), str(S), str(idf), str(lf), str(world),
+             str(rank), str(idfile), placement],
+            stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    for pr in procs:
+        out, _ = pr.communicate(timeout=300)
+        assert pr.returncode == 0, out
+    return [np.frombuffer(lf.read_bytes(), dtype=np.float32).reshape(B, V) for lf in outs]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("placement", ["balanced", "owner"])
+def test_cpp_model_ep_one_rank(cuda_dev, tiny_file, tmp_path, placement):
+    """LFM2Model(file, world=1, rank=0, id): the expert-parallel constructor
+    gives the replica model's logits bit for bit."""
+    _built()
+    p, _ = tiny_file
+    cfg = lc.TINY
+    B, S, V = cfg["batch"], cfg["seq"], cfg["vocab"]
+    ids = lc.token_ids(B, S, V, cfg["seed"])
+    want = _cpp_model_logits(p, ids, B, S, V, tmp_path / "single.f32")
+    (got,) = _cpp_model_ep(p, [ids], B, S, V, tmp_path, placement)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("placement", ["balanced", "owner"])
+def test_cpp_model_ep_two_ranks(cuda_dev, tiny_file, tmp_path, placement):
+    """Two processes, one per GPU, each with its own batch: each rank's
+    logits equal the single-GPU model's on the same ids, bit for bit."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _built()
+    p, _ = tiny_file
+    cfg = lc.TINY
+    B, S, V = cfg["batch"], cfg["seq"], cfg["vocab"]
+    ids = [lc.token_ids(B, S, V, cfg["seed"] + 7 * r) for r in range(2)]
+    want = [_cpp_model_logits(p, ids[r], B, S, V, tmp_path / f"single{r}.f32") for r in range(2)]
+    got = _cpp_model_ep(p, ids, B, S, V, tmp_path, placement)
+    for r in range(2):
+        assert np.array_equal(got[r].view(np.uint32), want[r].view(np.uint32)), r
