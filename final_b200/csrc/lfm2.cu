@@ -252,20 +252,20 @@ static b2_status norm_launch(float *resid, const float *delta, const float *w, i
                              int step, int off, int write_resid, float eps, float *y32,
                              __nv_bfloat16 *y16, cudaStream_t s) {
   if (rows <= 0) return B2_OK;
-  const dim3 g(rows), b(256);
+  const dim3 b(256), g1(rows), g2((rows + 1) / 2);
   switch (dim % 256 == 0 ? dim / 256 : 0) {
     case 8:
-      return launch_pdl(add_rmsnorm_kernel<8>, g, b, 0, s, resid, delta, w, dim, step, off,
-                        write_resid, eps, y32, y16);
+      return launch_pdl(add_rmsnorm_kernel<8, 2>, g2, b, 0, s, resid, delta, w, rows, dim, step,
+                        off, write_resid, eps, y32, y16);
     case 16:
-      return launch_pdl(add_rmsnorm_kernel<16>, g, b, 0, s, resid, delta, w, dim, step, off,
-                        write_resid, eps, y32, y16);
+      return launch_pdl(add_rmsnorm_kernel<16, 1>, g1, b, 0, s, resid, delta, w, rows, dim,
+                        step, off, write_resid, eps, y32, y16);
     case 4:
-      return launch_pdl(add_rmsnorm_kernel<4>, g, b, 0, s, resid, delta, w, dim, step, off,
-                        write_resid, eps, y32, y16);
+      return launch_pdl(add_rmsnorm_kernel<4, 2>, g2, b, 0, s, resid, delta, w, rows, dim, step,
+                        off, write_resid, eps, y32, y16);
     default:
-      return launch_pdl(add_rmsnorm_kernel<0>, g, b, 0, s, resid, delta, w, dim, step, off,
-                        write_resid, eps, y32, y16);
+      return launch_pdl(add_rmsnorm_kernel<0, 1>, g1, b, 0, s, resid, delta, w, rows, dim, step,
+                        off, write_resid, eps, y32, y16);
   }
 }
 

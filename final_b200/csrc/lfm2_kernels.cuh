@@ -43,10 +43,10 @@ static __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------ add + RMSNorm
-// One block of 256 threads per output row.  Input row = blockIdx.x * step +
-// off (step 1 / off 0 for every row; step S / off S-1 for the last token of
-// each sequence).  With ADD, v = resid + delta (written back to resid when
-// write_resid), else v = resid.  y = v * r * w with
+// One block of 256 threads per RPB output rows.  Input row of output row o =
+// o * step + off (step 1 / off 0 for every row; step S / off S-1 for the last
+// token of each sequence).  With ADD, v = resid + delta (written back to
+// resid when write_resid), else v = resid.  y = v * r * w with
 // r = 1 / sqrtf(sum(v^2) / dim + eps), written as fp32 and/or bf16.
 //
 // The sum is formed in exactly the order of the reference's rms_norm_kernel
@@ -54,74 +54,113 @@ static __global__ void __launch_bounds__(256)
 // FFMA, warps reduce by __shfl_down 16..1, warp 0 reduces the eight warp sums
 // by __shfl_down 4, 2, 1.  The division and square root are the IEEE ones
 // (no fast-math), so y equals the reference's bit for bit.
-// NPT > 0: dim == 256 * NPT, the row stays in registers (all NPT loads in
-// flight at once, no second read); NPT == 0: any dim, two passes.  Both sum
-// in the same order.
-template <int NPT>
+// NPT > 0: dim == 256 * NPT, the rows stay in registers: the RPB rows and the
+// weights are all loaded before the first reduction, so a block keeps
+// RPB * dim * 4 bytes in flight and its reduction latency is paid once for
+// RPB rows; each row is reduced in its own tree, in the order above.
+// NPT == 0 (RPB 1): any dim, two passes, the same order.
+template <int NPT, int RPB>
 __global__ void __launch_bounds__(256)
     add_rmsnorm_kernel(float *__restrict__ resid, const float *__restrict__ delta,
-                       const float *__restrict__ w, int dim, int step, int off, int write_resid,
-                       float eps, float *__restrict__ y32, __nv_bfloat16 *__restrict__ y16) {
+                       const float *__restrict__ w, int rows, int dim, int step, int off,
+                       int write_resid, float eps, float *__restrict__ y32,
+                       __nv_bfloat16 *__restrict__ y16) {
+  static_assert(NPT > 0 || RPB == 1, "the two-pass path handles one row per block");
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const size_t row_in = (size_t)blockIdx.x * step + off;
-  float *r = resid + row_in * dim;
-  const float *dl = delta ? delta + row_in * dim : nullptr;
-  float s = 0.0f;
-  float v[NPT > 0 ? NPT : 1];
+  __shared__ float ws[RPB][8];
+  __shared__ float total[RPB];
+  float s[RPB];
+  float v[RPB][NPT > 0 ? NPT : 1];
+  float wv[NPT > 0 ? NPT : 1];
+  bool ok[RPB];
+  float *r[RPB];
+  const float *dl[RPB];
+#pragma unroll
+  for (int q = 0; q < RPB; ++q) {
+    const int o = blockIdx.x * RPB + q;
+    ok[q] = o < rows;
+    const size_t row_in = (size_t)(ok[q] ? o : 0) * step + off;
+    r[q] = resid + row_in * dim;
+    dl[q] = delta ? delta + row_in * dim : nullptr;
+    s[q] = 0.0f;
+  }
   if constexpr (NPT > 0) {
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) v[j] = r[tid + 256 * j];
-    if (dl) {
+    for (int q = 0; q < RPB; ++q)
 #pragma unroll
-      for (int j = 0; j < NPT; ++j) v[j] = __fadd_rn(v[j], dl[tid + 256 * j]);
-      if (write_resid)
+      for (int j = 0; j < NPT; ++j) v[q][j] = ok[q] ? r[q][tid + 256 * j] : 0.0f;
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) r[tid + 256 * j] = v[j];
+    for (int j = 0; j < NPT; ++j) wv[j] = w[tid + 256 * j];
+    if (delta) {
+#pragma unroll
+      for (int q = 0; q < RPB; ++q) {
+        if (!ok[q]) continue;
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) v[q][j] = __fadd_rn(v[q][j], dl[q][tid + 256 * j]);
+        if (write_resid)
+#pragma unroll
+          for (int j = 0; j < NPT; ++j) r[q][tid + 256 * j] = v[q][j];
+      }
     }
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) s = __fmaf_rn(v[j], v[j], s);
+    for (int q = 0; q < RPB; ++q)
+#pragma unroll
+      for (int j = 0; j < NPT; ++j) s[q] = __fmaf_rn(v[q][j], v[q][j], s[q]);
   } else {
     for (int i = tid; i < dim; i += 256) {
-      float x = r[i];
-      if (dl) {
-        x = __fadd_rn(x, dl[i]);
-        if (write_resid) r[i] = x;
+      float x = r[0][i];
+      if (dl[0]) {
+        x = __fadd_rn(x, dl[0][i]);
+        if (write_resid) r[0][i] = x;
       }
-      s = __fmaf_rn(x, x, s);
+      s[0] = __fmaf_rn(x, x, s[0]);
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
-  __shared__ float ws[8];
-  __shared__ float total;
-  if (lane == 0) ws[warp] = s;
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int q = 0; q < RPB; ++q) s[q] += __shfl_down_sync(0xffffffffu, s[q], o);
+  if (lane == 0)
+#pragma unroll
+    for (int q = 0; q < RPB; ++q) ws[q][warp] = s[q];
   __syncthreads();
   if (warp == 0) {
-    float t = lane < 8 ? ws[lane] : 0.0f;
+    float t[RPB];
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) t += __shfl_down_sync(0xffffffffu, t, o);
-    if (lane == 0) total = t;
+    for (int q = 0; q < RPB; ++q) t[q] = lane < 8 ? ws[q][lane] : 0.0f;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+      for (int q = 0; q < RPB; ++q) t[q] += __shfl_down_sync(0xffffffffu, t[q], o);
+    if (lane == 0)
+#pragma unroll
+      for (int q = 0; q < RPB; ++q) total[q] = t[q];
   }
   __syncthreads();
-  const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)dim), eps)));
-  const size_t row_out = blockIdx.x;
-  if constexpr (NPT > 0) {
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) {
-      const int i = tid + 256 * j;
-      const float o = __fmul_rn(__fmul_rn(v[j], rms), w[i]);
-      if (y32) y32[row_out * dim + i] = o;
-      if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
-    }
-  } else {
-    for (int i = tid; i < dim; i += 256) {
-      float x = r[i];
-      if (dl && !write_resid) x = __fadd_rn(x, dl[i]);
-      const float o = __fmul_rn(__fmul_rn(x, rms), w[i]);
-      if (y32) y32[row_out * dim + i] = o;
-      if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+  for (int q = 0; q < RPB; ++q) {
+    if (!ok[q]) continue;
+    const float rms =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total[q], (float)dim), eps)));
+    const size_t row_out = (size_t)blockIdx.x * RPB + q;
+    if constexpr (NPT > 0) {
+#pragma unroll
+      for (int j = 0; j < NPT; ++j) {
+        const int i = tid + 256 * j;
+        const float o = __fmul_rn(__fmul_rn(v[q][j], rms), wv[j]);
+        if (y32) y32[row_out * dim + i] = o;
+        if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+      }
+    } else {
+      for (int i = tid; i < dim; i += 256) {
+        float x = r[q][i];
+        if (dl[q] && !write_resid) x = __fadd_rn(x, dl[q][i]);
+        const float o = __fmul_rn(__fmul_rn(x, rms), w[i]);
+        if (y32) y32[row_out * dim + i] = o;
+        if (y16) y16[row_out * dim + i] = __float2bfloat16_rn(o);
+      }
     }
   }
 }
@@ -132,12 +171,18 @@ __global__ void __launch_bounds__(256)
 // One block per token, one warp per head (lane l holds elements l and l+32,
 // which are exactly the pair RoPE rotates).  q / k heads: RMSNorm over the
 // 64 values in the reference's order for a 64-wide row (rms_norm_kernel,
-// src/layer.cu:144-191: two 32-lane shuffle trees, then their sum), then
-// RoPE at position s = t % S with the caller's [pos][64] cos / sin tables
+// src/layer.cu:144-191: two 32-lane shuffle trees, then their sum; the mean
+// x/64 is taken as x * 2^-6, the same correctly rounded value), then RoPE at
+// position s = t % S with the caller's [pos][64] cos / sin tables
 // (rope_transpose_kernel, :193-227):
 //   o1 = n1*c1 - n2*s1,  o2 = n2*c2 + n1*s2   (one FFMA each).
 // Written as bf16 in [B][heads][S][64] (one contiguous 128-byte row per
-// head and position), v heads converted only.
+// head and position), v heads converted only.  A warp loads all of its heads
+// (up to kQkHeadsInFlight) before computing any, so their HBM latencies
+// overlap instead of adding up head after head; the position's tables and
+// the two norm weights are loaded once per warp.
+constexpr int kQkHeadsInFlight = 8;  // per warp (48 heads over 8 warps: 6)
+
 static __global__ void __launch_bounds__(256)
     qk_norm_rope_kernel(const __nv_bfloat16 *__restrict__ qkv, const float *__restrict__ q_ln,
                         const float *__restrict__ k_ln, const float *__restrict__ cosv,
@@ -150,34 +195,50 @@ static __global__ void __launch_bounds__(256)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nh = Hq + 2 * Hkv;
   const __nv_bfloat16 *row = qkv + (size_t)t * nh * 64;
-  for (int h = warp; h < nh; h += 8) {
-    const float x1 = __bfloat162float(row[h * 64 + lane]);
-    const float x2 = __bfloat162float(row[h * 64 + lane + 32]);
-    __nv_bfloat16 *dst;
-    if (h >= Hq + Hkv) {
-      dst = v + (((size_t)b * Hkv + (h - Hq - Hkv)) * S + s) * 64;
-      dst[lane] = row[h * 64 + lane];
-      dst[lane + 32] = row[h * 64 + lane + 32];
-      continue;
-    }
-    float a = __fmul_rn(x1, x1), c = __fmul_rn(x2, x2);
+  const float *cs = cosv + (size_t)s * 64, *sn = sinv + (size_t)s * 64;
+  const float c1 = cs[lane], c2 = cs[lane + 32], s1 = sn[lane], s2 = sn[lane + 32];
+  const float wq1 = q_ln[lane], wq2 = q_ln[lane + 32];
+  const float wk1 = k_ln[lane], wk2 = k_ln[lane + 32];
+  for (int h0 = warp; h0 < nh; h0 += 8 * kQkHeadsInFlight) {
+    __nv_bfloat16 r1[kQkHeadsInFlight], r2[kQkHeadsInFlight];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      a += __shfl_down_sync(0xffffffffu, a, o);
-      c += __shfl_down_sync(0xffffffffu, c, o);
+    for (int j = 0; j < kQkHeadsInFlight; ++j) {
+      const int h = h0 + 8 * j;
+      if (h < nh) {
+        r1[j] = row[h * 64 + lane];
+        r2[j] = row[h * 64 + lane + 32];
+      }
     }
-    const float tot = __shfl_sync(0xffffffffu, __fadd_rn(a, c), 0);
-    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 64.0f), eps)));
-    const float *w = h < Hq ? q_ln : k_ln;
-    const float n1 = __fmul_rn(__fmul_rn(x1, rms), w[lane]);
-    const float n2 = __fmul_rn(__fmul_rn(x2, rms), w[lane + 32]);
-    const float *cs = cosv + (size_t)s * 64, *sn = sinv + (size_t)s * 64;
-    const float o1 = __fmaf_rn(n1, cs[lane], -__fmul_rn(n2, sn[lane]));
-    const float o2 = __fmaf_rn(n2, cs[lane + 32], __fmul_rn(n1, sn[lane + 32]));
-    dst = h < Hq ? q + (((size_t)b * Hq + h) * S + s) * 64
-                 : k + (((size_t)b * Hkv + (h - Hq)) * S + s) * 64;
-    dst[lane] = __float2bfloat16_rn(o1);
-    dst[lane + 32] = __float2bfloat16_rn(o2);
+#pragma unroll
+    for (int j = 0; j < kQkHeadsInFlight; ++j) {
+      const int h = h0 + 8 * j;  // warp-uniform
+      if (h >= nh) break;
+      if (h >= Hq + Hkv) {
+        __nv_bfloat16 *dst = v + (((size_t)b * Hkv + (h - Hq - Hkv)) * S + s) * 64;
+        dst[lane] = r1[j];
+        dst[lane + 32] = r2[j];
+        continue;
+      }
+      const float x1 = __bfloat162float(r1[j]);
+      const float x2 = __bfloat162float(r2[j]);
+      float a = __fmul_rn(x1, x1), c = __fmul_rn(x2, x2);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_down_sync(0xffffffffu, a, o);
+        c += __shfl_down_sync(0xffffffffu, c, o);
+      }
+      const float tot = __shfl_sync(0xffffffffu, __fadd_rn(a, c), 0);
+      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 0.015625f), eps)));
+      const bool isq = h < Hq;
+      const float n1 = __fmul_rn(__fmul_rn(x1, rms), isq ? wq1 : wk1);
+      const float n2 = __fmul_rn(__fmul_rn(x2, rms), isq ? wq2 : wk2);
+      const float o1 = __fmaf_rn(n1, c1, -__fmul_rn(n2, s1));
+      const float o2 = __fmaf_rn(n2, c2, __fmul_rn(n1, s2));
+      __nv_bfloat16 *dst = isq ? q + (((size_t)b * Hq + h) * S + s) * 64
+                               : k + (((size_t)b * Hkv + (h - Hq)) * S + s) * 64;
+      dst[lane] = __float2bfloat16_rn(o1);
+      dst[lane + 32] = __float2bfloat16_rn(o2);
+    }
   }
 }
 
