@@ -180,7 +180,8 @@ __global__ void __launch_bounds__(256)
 // head and position), v heads converted only.  A warp loads all of its heads
 // (up to kQkHeadsInFlight) before computing any, so their HBM latencies
 // overlap instead of adding up head after head; the position's tables and
-// the two norm weights are loaded once per warp.
+// the two norm weights are loaded once per warp, and the heads' 1/rms are
+// computed together (head j's sum in lane j).
 constexpr int kQkHeadsInFlight = 8;  // per warp (48 heads over 8 warps: 6)
 
 static __global__ void __launch_bounds__(256)
@@ -209,6 +210,26 @@ static __global__ void __launch_bounds__(256)
         r2[j] = row[h * 64 + lane + 32];
       }
     }
+    // sums of squares of the q / k heads, head j's in lane j, so one IEEE
+    // divide and square root serve all of them
+    float mine = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kQkHeadsInFlight; ++j) {
+      const int h = h0 + 8 * j;  // warp-uniform
+      if (h >= nh || h >= Hq + Hkv) break;
+      const float x1 = __bfloat162float(r1[j]);
+      const float x2 = __bfloat162float(r2[j]);
+      float a = __fmul_rn(x1, x1), c = __fmul_rn(x2, x2);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_down_sync(0xffffffffu, a, o);
+        c += __shfl_down_sync(0xffffffffu, c, o);
+      }
+      const float tot = __shfl_sync(0xffffffffu, __fadd_rn(a, c), 0);
+      if (lane == j) mine = tot;
+    }
+    const float rms_mine =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(mine, 0.015625f), eps)));
 #pragma unroll
     for (int j = 0; j < kQkHeadsInFlight; ++j) {
       const int h = h0 + 8 * j;  // warp-uniform
@@ -221,14 +242,7 @@ static __global__ void __launch_bounds__(256)
       }
       const float x1 = __bfloat162float(r1[j]);
       const float x2 = __bfloat162float(r2[j]);
-      float a = __fmul_rn(x1, x1), c = __fmul_rn(x2, x2);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        a += __shfl_down_sync(0xffffffffu, a, o);
-        c += __shfl_down_sync(0xffffffffu, c, o);
-      }
-      const float tot = __shfl_sync(0xffffffffu, __fadd_rn(a, c), 0);
-      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 0.015625f), eps)));
+      const float rms = __shfl_sync(0xffffffffu, rms_mine, j);
       const bool isq = h < Hq;
       const float n1 = __fmul_rn(__fmul_rn(x1, rms), isq ? wq1 : wk1);
       const float n2 = __fmul_rn(__fmul_rn(x2, rms), isq ? wq2 : wk2);
