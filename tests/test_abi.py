@@ -55,3 +55,25 @@ def test_no_fallback_without_library(tmp_path):
             _lib.load(tmp_path / "libb2moe.so")
     finally:
         _lib._lib = saved
+
+
+def test_new_entry_points_reject_bad_arguments():
+    """Argument checks that return before any device work (no GPU needed)."""
+    import ctypes as C
+    from final_b200 import _lib
+    lib = _lib.load()
+    n = C.c_int(0)
+    assert lib.b2_ep_profile_timeline(None, 0, None, None, C.byref(n)) == _lib.B2_ERR_INVALID
+    assert lib.b2_lfm2_set_timeout(None, 1.0) == _lib.B2_ERR_INVALID
+    d = _lib.Lfm2Desc(vocab=300, hidden=256, num_layers=5, num_heads=4, num_kv_heads=2,
+                      dense_inter=384, moe_inter=128, num_experts=8, top_k=4,
+                      num_dense_layers=2, max_batch=2, max_seq=8)
+    h = C.c_void_p()
+    uid = C.create_string_buffer(128)
+    fn = _lib.WEIGHT_FN(lambda ctx, name, numel: None)
+    # world / rank / mode out of range, no id, experts not divisible among owners
+    for world, rank, mode, u in ((0, 0, 1, uid), (2, 2, 1, uid), (2, 0, 7, uid),
+                                 (2, 0, 1, None), (3, 0, 0, uid)):
+        assert lib.b2_lfm2_create_ep(C.byref(d), fn, None, 1, world, rank, u, mode, None,
+                                     C.byref(h)) == _lib.B2_ERR_INVALID
+    assert not h.value
