@@ -265,3 +265,32 @@ def test_ep_two_gloo_ranks_match_single_rank(oracle, mode):
         assert p.exitcode == 0
     y = np.concatenate([got[0], got[1]])
     assert np.array_equal(y.view(np.uint32), ref["y"].view(np.uint32))
+
+
+@pytest.mark.parametrize("world", [16, 64])
+def test_plan_balanced_edge_cases(world):
+    """Large worlds, no rows at all, every row on one rank, one hot expert:
+    shares cover the rows exactly once, match the restated boundaries, and
+    stay within the receive capacity (3/2 of the mean rows, +1)."""
+    E = 32
+    rng = np.random.default_rng(world)
+    cases = [np.zeros((world, E), np.int32)]
+    one_rank = np.zeros((world, E), np.int32)
+    one_rank[world // 2] = rng.integers(0, 500, size=E)
+    cases.append(one_rank)
+    hot = np.zeros((world, E), np.int32)
+    hot[:, 7] = rng.integers(1, 3000, size=world)
+    cases.append(hot)
+    cases.append(rng.integers(0, 40, size=(world, E)).astype(np.int32))
+    for cnt in cases:
+        plans = [epmod.plan(cnt, r, "balanced") for r in range(world)]
+        R = int(cnt.sum())
+        rows = [p["recv_rows"] for p in plans]
+        assert sum(rows) == R
+        assert rows == _balanced_rows(cnt)
+        for n in rows:
+            assert n <= R / world * 1.5 + 1
+        for r, p in enumerate(plans):
+            assert sum(p["send_cnt"]) == int(cnt[r].sum())
+            for s in range(world):
+                assert plans[s]["send_cnt"][r] == p["recv_cnt"][s]
