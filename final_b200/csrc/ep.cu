@@ -705,7 +705,15 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
     return sc;
   };
 
-  // 3. dispatch on the copy engine: step k pushes the rows for rank r+k into
+  // 3. first part of the own rows, in place (sorted_x -> inter -> sout), while
+  // rows travel.  Launched before the host enqueues the 2(G-1) dispatch
+  // copies, which wait on ev_ready either way, so the GPU does not idle while
+  // the host issues them.
+  if (nseg[r] > 0)
+    B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(r), s,
+                                false));
+  B2_RETURN_IF(tl(B2_EP_TL_OWN_FIRST));
+  // 4. dispatch on the copy engine: step k pushes the rows for rank r+k into
   // its receive buffer, then our sequence number into its flag slot
   const char *sx = reinterpret_cast<const char *>(m->sorted_x);
   B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_ready, 0));
@@ -718,11 +726,6 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
     B2_CUDA(cudaMemcpyAsync(ep->peer_flags[to] + kFlagDispatch * G + r, ep->d_seq,
                             sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_d));
   }
-  // 4. first part of the own rows, in place (sorted_x -> inter -> sout), while rows travel
-  if (nseg[r] > 0)
-    B2_RETURN_IF(moe_gemm_stage(m, m->tm_x, ep->tm_inter, ep->inter, m->sout, sched_of(r), s,
-                                false));
-  B2_RETURN_IF(tl(B2_EP_TL_OWN_FIRST));
   // 5. per step: wait for the rows of rank r-k, expert GEMMs, return them
   const char *ro = reinterpret_cast<const char *>(ep->out_recv);
   for (int k = 1; k < G; ++k) {
