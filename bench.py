@@ -59,8 +59,10 @@ def parse():
                    help="only time the full-model forward (config 5)")
     p.add_argument("--model-ep", choices=["none", "balanced", "owner"], default="balanced",
                    help="with several GPUs, also time the expert-parallel model in this mode")
-    p.add_argument("--ep-mode", choices=["balanced", "owner"], default="balanced",
-                   help="expert placement when --gpus > 1")
+    p.add_argument("--ep-mode", choices=["balanced", "owner"], default="owner",
+                   help="expert placement when --gpus > 1 (owner: E/N experts per GPU)")
+    p.add_argument("--no-variants", action="store_true",
+                   help="with --gpus > 1, skip the other placements / routings / pipeline")
     p.add_argument("--gemm-configs", type=int, nargs=3, metavar=("M", "N", "K"),
                    help="time every dense-GEMM kernel configuration on one shape (bf16)")
     p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
@@ -243,38 +245,69 @@ def layer_flop(T):
 
 
 # ------------------------------------------------------------------ ours
-def run_ours(args, rank, world, dev):
+def bench_config(args, world):
+    """The workload the line measures -- a function of the arguments alone, so
+    the reference arm prints the identical dict."""
+    T = args.tokens
+    return {"workload": f"moe_layer_{T // 1024}k_{args.routing}", "tokens_per_gpu": T,
+            "hidden": H, "experts": E, "top_k": K, "inter": I,
+            "routing": ("zipf(1.1) injected logits" if args.routing == "zipf"
+                        else "x.gate N(0,1)xN(0,0.02), bias N(0,0.02)"),
+            "l2": "inputs larger than L2: x 134 MB fp32, expert weights 705 MB bf16",
+            "parallelism": (f"expert-parallel ep{world} ({args.ep_mode} placement), fused "
+                            "grouped GEMMs with peer-memory dispatch/return, NCCL count "
+                            "all-gather" if world > 1 else "single")}
+
+
+def exchange_bytes(plan, rank, world, row_bytes):
+    """Bytes this rank moved over NVLink in one forward, from its plan."""
+    sent = sum(c for d, c in enumerate(plan["send_cnt"]) if d != rank)
+    recv = sum(c for s, c in enumerate(plan["recv_cnt"]) if s != rank)
+    return {"rank": rank, "rows_computed": plan["recv_rows"],
+            "dispatch_sent": sent * row_bytes, "dispatch_received": recv * row_bytes,
+            "return_sent": recv * row_bytes, "return_received": sent * row_bytes}
+
+
+def time_layer(args, rank, world, dev, mode, routing, pipeline="fused", e2e=False,
+               keep_host=False):
+    """One MoE layer (single-GPU, or expert-parallel over `world` ranks in
+    `mode` placement) on `routing` inputs: W warm-up forwards, then K
+    forwards timed with CUDA events between barriers (max over ranks), a
+    second K-forward pass with stage events, and optionally the end-to-end
+    pass through host buffers.  Returns the measurements."""
     import torch
     import torch.distributed as dist
     from final_b200 import SparseMoeBlock, launch_count
 
     T = args.tokens
-    x, gate, bias, w1, w2, w3 = make_inputs(T, args.routing, dev, SEED, SEED + 1000 * (rank + 1))
+    x, gate, bias, w1, w2, w3 = make_inputs(T, routing, dev, SEED, SEED + 1000 * (rank + 1))
     if world > 1:
         from final_b200.ep import ExpertParallelMoE
         layer = ExpertParallelMoE(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype,
-                                  mode=args.ep_mode, timeout_s=120.0)
+                                  mode=mode, timeout_s=120.0, pipeline=pipeline)
     else:
         layer = SparseMoeBlock(gate, w1, w2, w3, bias, max_tokens=T, top_k=K, dtype=args.dtype)
-    w_host = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    res = {}
+    if keep_host:
         # fp32 weights for the CPU baseline sample (same workload)
-        w_host = [t.cpu().numpy() for t in (w1, w3, w2)]
-        cpu_inputs = (x.cpu().numpy(), gate.cpu().numpy(),
-                      None if bias is None else bias.cpu().numpy())
+        res["host"] = ([t.cpu().numpy() for t in (w1, w3, w2)],
+                       (x.cpu().numpy(), gate.cpu().numpy(),
+                        None if bias is None else bias.cpu().numpy()))
     del w1, w2, w3
     torch.cuda.empty_cache()
     y = torch.empty(T, H, device=dev)
+    row_bytes = H * (4 if args.dtype == "tf32" else 2)
     if world > 1:
         layer.forward_gpu(x, y, T)
         torch.cuda.synchronize()
         plan = layer.last_plan()
-        rows = torch.tensor([plan["recv_rows"]], device=dev)
-        all_rows = [torch.zeros_like(rows) for _ in range(world)]
-        dist.all_gather(all_rows, rows)
-        counts_probe = [int(r.item()) for r in all_rows]   # rows each rank computes
+        ex = [None] * world
+        dist.all_gather_object(ex, exchange_bytes(plan, rank, world, row_bytes))
+        res["exchange_bytes_per_step"] = ex
+        res["load"] = {"rows_per_rank": [e["rows_computed"] for e in ex]}
     else:
-        counts_probe = layer.forward_traced(x)["counts"].cpu().tolist()
+        cnt = layer.forward_traced(x)["counts"].cpu().tolist()
+        res["load"] = {"expert_rows_max_min": [max(cnt), min(cnt)]}
 
     stream = torch.cuda.current_stream()
     fwd = (lambda xi, yi: layer.forward_gpu(xi, yi, T, stream)) if world > 1 else \
@@ -298,8 +331,8 @@ def run_ours(args, rank, world, dev):
         fwd(x, y)
     ev1.record(stream)
     torch.cuda.synchronize()
-    clocks = sampler.stop()
-    n1 = launch_count()
+    res["clocks"] = sampler.stop()
+    res["gpu_launches"] = int(launch_count() - n0)
     if world > 1:
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
@@ -311,11 +344,11 @@ def run_ours(args, rank, world, dev):
         fwd(x, y)
     torch.cuda.synchronize()
     layer.profile(False)
-    stage_ms, nfw = layer.profile_read()
-    timeline = None
+    res["stage_ms"], res["nfw"] = layer.profile_read()
     if world > 1:
-        timeline = [None] * world
-        dist.all_gather_object(timeline, layer.timeline())
+        tl = [None] * world
+        dist.all_gather_object(tl, layer.timeline())
+        res["timeline"] = tl
         dist.barrier()
     st = layer.device_status()
     if st != 0:
@@ -324,13 +357,15 @@ def run_ours(args, rank, world, dev):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
+    res["ms"] = ms
+    res["ms_per_step"] = ms / args.steps
+    res["value"] = T * args.steps * world / (ms / 1e3)
 
     # ---- end-to-end through the public API with host buffers: every step
     # copies its input batch from pinned host memory and its result back;
     # copies of step i+1 / i-1 overlap the layer of step i (two copy streams,
     # double-buffered device buffers).
-    e2e = None
-    if not args.no_e2e:
+    if e2e:
         xh = x.cpu().pin_memory()
         yh = [torch.empty(T, H, dtype=torch.float32).pin_memory() for _ in range(2)]
         xd = [torch.empty_like(x) for _ in range(2)]
@@ -376,20 +411,34 @@ def run_ours(args, rank, world, dev):
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = t.item()
-        e2e = {"value": T * args.steps * world / (ems / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-               "ms_per_step": ems / args.steps,
-               "how": "pinned host x -> device, layer, device y -> pinned host every step; "
-                      "copies overlap neighbouring steps' layers on two copy streams"}
+        res["e2e"] = {"value": T * args.steps * world / (ems / 1e3), "unit": "tokens/s",
+                      "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                      "ms_per_step": ems / args.steps,
+                      "how": "pinned host x -> device, layer, device y -> pinned host every "
+                             "step; copies overlap neighbouring steps' layers on two copy "
+                             "streams"}
+    layer.close()
+    del layer, x, y
+    torch.cuda.empty_cache()
+    return res
 
+
+def run_ours(args, rank, world, dev):
+    T = args.tokens
+    keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline
+    head = time_layer(args, rank, world, dev, args.ep_mode, args.routing, e2e=not args.no_e2e,
+                      keep_host=keep_host)
+    stage_ms, nfw = head["stage_ms"], head["nfw"]
     pk = peaks()
     flop = layer_flop(T)
-    value = T * args.steps * world / (ms / 1e3)
+    ms = head["ms"]
+    value = head["value"]
     gemm_flop = T * K * 6 * H * I
     w13_flop = T * K * 4 * H * I
     w13_ms = stage_ms["gemm_w13"] / max(nfw, 1)
     w2_ms = stage_ms["gemm_w2"] / max(nfw, 1)
     achieved = w13_flop / (w13_ms / 1e3) / 1e12
+    clocks = head["clocks"]
     # denominator: the burst cuBLAS figure when the SM clock stayed at its
     # maximum through the timed region, the power-capped sustained figure if not
     at_max = bool(clocks) and clocks["sm_mhz"] >= 0.95 * clocks["sm_max_mhz"]
@@ -407,38 +456,47 @@ def run_ours(args, rank, world, dev):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
-        "config": {"workload": f"moe_layer_{T // 1024}k_{args.routing}", "tokens_per_gpu": T,
-                   "hidden": H, "experts": E, "top_k": K, "inter": I,
-                   "routing": ("zipf(1.1) injected logits" if args.routing == "zipf"
-                               else "x.gate N(0,1)xN(0,0.02), bias N(0,0.02)"),
-                   ("rows_per_rank" if world > 1 else "expert_load_max_min"):
-                       counts_probe if world > 1 else [max(counts_probe), min(counts_probe)],
-                   "weights": f"{args.dtype} packed from fp32 N(0,0.02)",
-                   "l2": "inputs larger than L2: x 134 MB fp32, expert weights 705 MB bf16",
-                   "parallelism": (f"expert-parallel ep{world} ({args.ep_mode}), copy-engine peer "
-                                   "dispatch/combine, NCCL count all-gather"
-                                   if world > 1 else "single")},
+        "config": bench_config(args, world),
+        "weights": f"{args.dtype} packed from fp32 N(0,0.02), random init",
+        "load": head["load"],
         "layer_tflops": flop * args.steps * world / (ms / 1e3) / 1e12 / world,
         "grouped_gemm_tflops": gemm_flop / ((w13_ms + w2_ms) / 1e3) / 1e12,
         "frac_of_bf16_peak_layer": flop / (ms / args.steps / 1e3) / 1e12 / pk["bf16"],
         "stages_ms_per_step": {k: v / max(nfw, 1) for k, v in stage_ms.items()},
-        **({"ep_timeline_us": timeline} if timeline else {}),
         "roofline": {"kernel": "gemm_pair_kernel<SwiGLU,bf16> (W1||W3 grouped GEMM, CTA pairs)",
                      "bound": "tensor", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_kind": peak_kind,
                      "flop_per_launch": w13_flop},
-        "gpu_launches": int(n1 - n0),
+        "gpu_launches": head["gpu_launches"],
         "clocks": clocks,
     }
-    if e2e:
-        out["e2e"] = e2e
+    if world > 1:
+        out["roofline"]["note"] = ("expert-parallel: the W1||W3 stage time includes waiting "
+                                   "for remote rows; the 1-GPU line is the kernel figure")
+        out["exchange_bytes_per_step"] = head["exchange_bytes_per_step"]
+        out["ep_timeline_us"] = head["timeline"]
+        if not args.no_variants:
+            # the other placements / routings of the same layer, same K / W
+            var = {}
+            combos = [(m, r, "fused") for m in ("owner", "balanced") for r in ("zipf", "uniform")]
+            combos.append((args.ep_mode, args.routing, "staged"))
+            for mode, routing, pipe in combos:
+                key = f"{mode}_{routing}_{pipe}"
+                if (mode, routing, pipe) == (args.ep_mode, args.routing, "fused"):
+                    continue
+                r = time_layer(args, rank, world, dev, mode, routing, pipe)
+                var[key] = {"value": r["value"], "ms_per_step": r["ms_per_step"],
+                            "load": r["load"], "timeline_rank0_us": r["timeline"][0]}
+            out["variants"] = var
+    if "e2e" in head:
+        out["e2e"] = head["e2e"]
     if not args.no_dense and rank == 0:
         out["dense_gemm_sweep"] = dense_sweep(dev)
         out["dense_mlp"] = mlp_bench(dev)
     if not args.no_model:
-        del layer
+        import torch
         torch.cuda.empty_cache()
         fm = model_bench(dev, rank=rank, world=world)
         if rank == 0:
@@ -447,7 +505,8 @@ def run_ours(args, rank, world, dev):
             fm = model_bench(dev, rank=rank, world=world, ep=args.model_ep)
             if rank == 0:
                 out["full_model_ep"] = fm
-    if w_host is not None:
+    if "host" in head:
+        w_host, cpu_inputs = head["host"]
         out["cpu_baseline"] = cpu_baseline(args, cpu_inputs, w_host)
     return out
 
@@ -777,8 +836,7 @@ def run_reference(args):
            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": f"moe_layer_{T // 1024}k_{args.routing}", "tokens_per_gpu": T,
-                      "hidden": H, "experts": E, "top_k": K, "inter": I},
+           "config": bench_config(args, args.gpus),
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                             "sample": f"{n} tokens per step of the {T}-token workload "
                                       "(C restatement of src/layer.cu MoE, fp32, OpenMP)"},

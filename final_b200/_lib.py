@@ -20,10 +20,11 @@ EXPORTED = (
     "b2_moe_get_status", "b2_moe_tile_rows", "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_device_bytes", "b2_gemm_nt", "b2_convert_f32_to_bf16",
     "b2_gemm_plan", "b2_gemm_nt_config",
     "b2_kernel_launch_count", "b2_status_string", "b2_version", "b2_moe_route_noalloc",
+    "b2_device_code_version", "b2_moe_dispatch_slots",
     # include/b2moe_ep.h
     "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
     "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_layer", "b2_ep_destroy", "b2_flag_wait",
-    "b2_ep_profile_timeline",
+    "b2_ep_profile_timeline", "b2_ep_set_pipeline", "b2_ep_fused_schedule",
     # include/b2mlp.h
     "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_device_bytes",
     "b2_mlp_destroy",
@@ -143,6 +144,8 @@ def load(path: Path | None = None):
                                  C.POINTER(vp)]
     lib.b2_ep_forward.argtypes = [vp, vp, vp, i, vp]
     lib.b2_ep_set_timeout.argtypes = [vp, C.c_double]
+    lib.b2_ep_set_pipeline.argtypes = [vp, i]
+    lib.b2_ep_fused_schedule.argtypes = [i, i, i, i, vp, i, vp, C.POINTER(i), C.POINTER(i)]
     lib.b2_flag_wait.argtypes = [vp, vp, i, C.c_uint64, C.c_double, vp, vp]
     lib.b2_ep_last_plan.argtypes = [vp, C.POINTER(EpPlan)]
     lib.b2_ep_profile_timeline.argtypes = [vp, i, C.POINTER(i), C.POINTER(C.c_float),
@@ -202,12 +205,16 @@ def load(path: Path | None = None):
     lib.b2_status_string.argtypes = [i]
     lib.b2_status_string.restype = C.c_char_p
     lib.b2_version.restype = C.c_char_p
+    lib.b2_device_code_version.argtypes = [C.POINTER(i)]
+    lib.b2_moe_dispatch_slots.argtypes = [vp, vp, i, vp, vp, vp, vp]
+    lib.b2_device_code_version.restype = i
     for name in ("b2_moe_create", "b2_moe_destroy", "b2_moe_forward", "b2_moe_forward_ex",
                  "b2_moe_get_status", "b2_gemm_nt", "b2_convert_f32_to_bf16",
                  "b2_moe_profile_enable", "b2_moe_profile_read", "b2_moe_route_noalloc",
+                 "b2_moe_dispatch_slots",
                  "b2_ep_plan_compute", "b2_ep_unique_id", "b2_ep_create", "b2_ep_forward",
                  "b2_ep_set_timeout", "b2_ep_last_plan", "b2_ep_destroy", "b2_flag_wait",
-                 "b2_ep_profile_timeline",
+                 "b2_ep_profile_timeline", "b2_ep_set_pipeline", "b2_ep_fused_schedule",
                  "b2_mlp_create", "b2_mlp_forward", "b2_mlp_get_status", "b2_mlp_destroy"):
         getattr(lib, name).restype = i
     _lib = lib

@@ -92,9 +92,23 @@ def build_cpp(force: bool = False, verbose: bool = False) -> None:
         subprocess.run(cmd, check=True)
 
 
+def reference_dir():
+    """The reference checkout whose kernels oracle/_ref is compiled from: the
+    B2_REFERENCE_DIR environment variable, else a directory named
+    ``reference`` beside this repository; None when neither holds
+    src/layer.cu (e.g. on a GPU box, which uses the prebuilt oracle/_ref)."""
+    for cand in (os.environ.get("B2_REFERENCE_DIR"), ROOT.parent / "reference"):
+        if cand and (Path(cand) / "src" / "layer.cu").is_file():
+            return Path(cand)
+    return None
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Build the CPU oracle (and oracle/_ref when the reference tree exists)."""
     cmd = ["make", "-C", str(ROOT / "oracle")]
+    ref = reference_dir()
+    if ref is not None:
+        cmd.append(f"REF={ref}")
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True, stdout=None if verbose else subprocess.DEVNULL)

@@ -387,7 +387,8 @@ extern "C" b2_status b2_moe_forward_ex(b2_moe *m, const float *x, float *y, int 
 
 b2_status b2::moe_forward_impl(b2_moe *m, const float *x, float *y, int T,
                                const b2_moe_trace *tr, cudaStream_t s, bool accumulate) {
-  if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (!m || T < 0 || (T > 0 && (!x || !y || !aligned16(x) || !aligned16(y))))
+    return B2_ERR_INVALID;
   if (m->n_wexp != m->d.num_experts || !m->inter) return B2_ERR_INVALID;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   if (T == 0) return B2_OK;
@@ -421,6 +422,36 @@ b2_status b2::moe_forward_impl(b2_moe *m, const float *x, float *y, int T,
 extern "C" b2_status b2_moe_forward(b2_moe *m, const float *x, float *y, int T,
                                     b2_stream stream) {
   return b2_moe_forward_ex(m, x, y, T, nullptr, stream);
+}
+
+extern "C" b2_status b2_moe_dispatch_slots(b2_moe *m, const int32_t *topk_idx, int T,
+                                           int32_t *counts, int32_t *offsets,
+                                           int32_t *token_slot, b2_stream stream_) {
+  if (!m || T < 0 || (T > 0 && (!topk_idx || !token_slot))) return B2_ERR_INVALID;
+  if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
+  const int E = m->d.num_experts, K = m->d.top_k;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  if (T == 0) {
+    if (counts) B2_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, s));
+    if (offsets) B2_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * E, s));
+    return B2_OK;
+  }
+  const int nb = (T + kRouteTB - 1) / kRouteTB;
+  B2_RETURN_IF(launch_pdl(hist_kernel, dim3(nb), dim3(128), 0, s, topk_idx, T, E, K,
+                          m->block_counts));
+  B2_RETURN_IF(launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, s, (const int *)m->block_counts, nb,
+                          E, (int)kPairBM, m->counts, m->offsets, m->mtile, m->block_base));
+  // slot bookkeeping only (hidden 0: no row copy); bad ids are recorded here
+  B2_RETURN_IF(launch_pdl(scatter_kernel<__nv_bfloat16>, dim3(nb), dim3(scatter_threads(K)), 0, s,
+                          (const float *)nullptr, topk_idx, (const float *)nullptr,
+                          (const int *)m->block_base, T, 0, E, K, (__nv_bfloat16 *)nullptr,
+                          token_slot, (int *)nullptr, (float *)nullptr, m->status));
+  if (counts)
+    B2_CUDA(cudaMemcpyAsync(counts, m->counts, sizeof(int32_t) * E, cudaMemcpyDeviceToDevice, s));
+  if (offsets)
+    B2_CUDA(
+        cudaMemcpyAsync(offsets, m->offsets, sizeof(int32_t) * E, cudaMemcpyDeviceToDevice, s));
+  return B2_OK;
 }
 
 extern "C" b2_status b2_moe_get_status(b2_moe *m, b2_stream stream_, int *device_status) {
@@ -562,3 +593,11 @@ extern "C" const char *b2_status_string(b2_status s) {
 }
 
 extern "C" const char *b2_version(void) { return "b2moe sm_100a tcgen05 v0.2"; }
+
+extern "C" b2_status b2_device_code_version(int *version) {
+  if (!version) return B2_ERR_INVALID;
+  cudaFuncAttributes a{};
+  B2_CUDA(cudaFuncGetAttributes(&a, reinterpret_cast<const void *>(scan_kernel)));
+  *version = a.binaryVersion;
+  return B2_OK;
+}

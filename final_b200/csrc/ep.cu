@@ -10,12 +10,18 @@
 //   3. dispatch: the copy engine pushes each peer's contiguous chunk of bf16
 //      rows straight into that peer's receive buffer (CUDA IPC mapping over
 //      NVLink), followed by a sequence-number flag -- no SMs are used;
-//   4. the rank's own rows go through the two grouped tcgen05 GEMMs in place
-//      while rows travel; then, per source, a bounded flag wait and the GEMMs
-//      on what arrived;
-//   5. return: each source's results go back the same way into the source's
-//      sout at the rows they came from, so the local k-ordered combine
-//      (moe_combine_stage) reads them unchanged.
+//   4. fused pipeline (default): ONE W1||W3 launch over the rank's own rows
+//      and every source's rows -- the TMA producer of a tile from source s
+//      waits (bounded) on s's arrival flag before loading it, so the GEMM
+//      starts on the own rows at once and takes each source as it lands --
+//      and ONE W2 launch whose epilogue stores each row's result straight into
+//      the sout of the rank the row came from (peer stores over NVLink); a
+//      signal kernel then raises this rank's return flag at every source.
+//      Staged pipeline: the own rows in place, then per source a bounded flag
+//      wait and a W1||W3 + W2 launch pair, results returned by the copy
+//      engine;
+//   5. after every source has signalled, the local k-ordered combine
+//      (moe_combine_stage) reads sout unchanged.
 // NCCL (loaded at run time: the process's libnccl.so.2, normally PyTorch's, so
 // the library has no link-time NCCL dependency) carries only the per-forward
 // all-gather of the expert counts and the start-up exchange of IPC handles.
@@ -25,6 +31,7 @@
 
 #include <chrono>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <thread>
 
@@ -290,6 +297,11 @@ struct b2_ep {
   std::vector<uint64_t *> peer_flags;
   int *d_wait_idx = nullptr, *h_wait_idx = nullptr;
   CUtensorMap tm_recv, tm_inter;
+  int64_t inter_rows = 0;
+  int pipeline = B2_EP_PIPE_FUSED;
+  void **d_out_ptrs = nullptr;         // [world]: sout of every rank (own, peers over IPC)
+  uint64_t **d_ret_flags = nullptr;    // [world-1]: our return-flag slot at each peer
+  int32_t *d_fsched = nullptr, *h_fsched = nullptr;  // fused schedules: W1||W3, then W2
   int32_t *d_cnt_all = nullptr, *h_cnt_all = nullptr;
   int32_t *d_sched = nullptr, *h_sched = nullptr;  // per source: counts|offsets|mtile|group_b
   std::vector<b2_ep_plan> plans;                   // every rank's plan of the last forward
@@ -302,6 +314,18 @@ struct b2_ep {
 };
 
 static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
+// a fused schedule: counts | C rows | m-tile prefix | expert | A rows | source | destination
+static constexpr int kFusedSchedInts = kPairSchedArrays * (kMaxGroups + 1);
+
+// Raises this rank's flag at every peer once the preceding W2 launch (whose
+// epilogue stored the peers' rows into their sout) has completed: a plain
+// stream-ordered launch, so every store of that grid has been performed
+// before the release stores below.
+static __global__ void signal_flags_kernel(uint64_t *const *flag_ptrs, int n, uint64_t value) {
+  __threadfence_system();
+  const int i = threadIdx.x;
+  if (i < n) st_release_sys(flag_ptrs[i], value);
+}
 
 // Bounded wait, on this GPU, for flags[idx[i]] >= target (one lane per flag).
 // Gives up after timeout_ns, recording kDevTimeoutPeer in *status.  Launched
@@ -429,6 +453,7 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   if (ep->h_sched) cudaFreeHost(ep->h_sched);
   if (ep->h_seq) cudaFreeHost(ep->h_seq);
   if (ep->h_wait_idx) cudaFreeHost(ep->h_wait_idx);
+  if (ep->h_fsched) cudaFreeHost(ep->h_fsched);
   b2_moe_destroy(ep->moe);  // also frees the buffers registered with it
   delete ep;
   return B2_OK;
@@ -470,6 +495,7 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
   ep->cap_rows =
       mode == B2_EP_OWNER ? local_rows * world : local_rows + local_rows / 2 + world + 1;
   const int64_t inter_rows = std::max<int64_t>(ep->cap_rows, local_rows);
+  ep->inter_rows = inter_rows;
   auto fail = [&](b2_status s) {
     b2_ep_destroy(ep);
     return s;
@@ -487,10 +513,17 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
   if ((st = moe_alloc(m, (void **)&ep->d_sched, sizeof(int32_t) * kSchedInts * (world + 1))) !=
       B2_OK)
     return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_fsched, sizeof(int32_t) * 2 * kFusedSchedInts)) != B2_OK)
+    return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_out_ptrs, sizeof(void *) * world)) != B2_OK)
+    return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_ret_flags, sizeof(void *) * world)) != B2_OK)
+    return fail(st);
   if (cudaMallocHost(&ep->h_cnt_all, sizeof(int32_t) * world * kMaxExperts) != cudaSuccess ||
       cudaMallocHost(&ep->h_sched, sizeof(int32_t) * kSchedInts * (world + 1)) != cudaSuccess ||
       cudaMallocHost(&ep->h_seq, sizeof(uint64_t)) != cudaSuccess ||
-      cudaMallocHost(&ep->h_wait_idx, sizeof(int) * 2 * world) != cudaSuccess)
+      cudaMallocHost(&ep->h_wait_idx, sizeof(int) * 2 * world) != cudaSuccess ||
+      cudaMallocHost(&ep->h_fsched, sizeof(int32_t) * 2 * kFusedSchedInts) != cudaSuccess)
     return fail(B2_ERR_CUDA);
   if (cudaMemsetAsync(ep->inter, 0, es * inter_rows * Ip, stream) != cudaSuccess ||
       cudaMemsetAsync(ep->flags, 0, sizeof(uint64_t) * 2 * world, stream) != cudaSuccess)
@@ -570,6 +603,21 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
       ep->peer_flags[p] = static_cast<uint64_t *>(ptr);
     }
   }
+  // output bases of the fused W2 (every rank's sout) and this rank's
+  // return-flag slot at each peer, in exchange-step order
+  {
+    std::vector<void *> outs(world), rets(world, nullptr);
+    for (int p = 0; p < world; ++p) outs[p] = p == rank ? m->sout : ep->peer_sout[p];
+    for (int k = 1; k < world; ++k) {
+      const int from = (rank - k + world) % world;
+      rets[k - 1] = ep->peer_flags[from] + kFlagReturn * world + rank;
+    }
+    if (cudaMemcpy(ep->d_out_ptrs, outs.data(), sizeof(void *) * world,
+                   cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(ep->d_ret_flags, rets.data(), sizeof(void *) * world,
+                   cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(B2_ERR_CUDA);
+  }
   *out = ep;
   return B2_OK;
 }
@@ -610,16 +658,204 @@ static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self
   return n;
 }
 
+// Schedule of one fused launch (every source's rows), into h (kFusedSchedInts
+// ints).  W1||W3 (w2 = false): the own rows first -- A = sorted_x at their
+// expert-sorted rows, so the GEMM starts at once -- then the sources in the
+// order their rows arrive (rank s pushes to s+1 first, so r-1, r-2, ...), A =
+// the receive buffer behind that source's flag; C = the receive-layout row
+// (inter).  W2 (w2 = true): the remote sources first and the own rows last
+// (their results need no NVLink, so the last stores of the launch stay
+// local); A = the inter row; C = the row's expert-sorted position at its
+// source, destination = the source.  Within a source the groups keep the
+// plan's expert order.  Returns the number of groups; *mtiles the m-tiles.
+static int fill_fused(int G, int r, const b2_ep_plan *plans, bool w2, int32_t *h, int *mtiles) {
+  constexpr int N1 = kMaxGroups + 1;
+  const b2_ep_plan &p = plans[r];
+  int32_t *hc = h, *ho = h + N1, *hm = h + 2 * N1, *hg = h + 3 * N1, *ha = h + 4 * N1,
+          *hs = h + 5 * N1, *hd = h + 6 * N1;
+  int n = 0, mt = 0;
+  for (int k = 0; k < G; ++k) {
+    const int src = w2 ? (k < G - 1 ? (r - 1 - k + 2 * G) % G : r) : (r - k + G) % G;
+    for (int g = 0; g < p.num_segments; ++g) {
+      if (p.seg_source[g] != src) continue;
+      const int64_t within = p.seg_off[g] - p.recv_off[src];
+      const int64_t home = plans[src].send_off[r] + within;  // its row at the source
+      hc[n] = p.seg_cnt[g];
+      hg[n] = p.seg_expert[g];
+      if (!w2) {
+        ho[n] = p.seg_off[g];
+        ha[n] = (int32_t)(src == r ? home : p.seg_off[g]);
+        hs[n] = src == r ? -1 : src;
+        hd[n] = 0;
+      } else {
+        ho[n] = (int32_t)home;
+        ha[n] = p.seg_off[g];
+        hs[n] = -1;
+        hd[n] = src;
+      }
+      hm[n] = mt;
+      mt += (p.seg_cnt[g] + kPairBM - 1) / kPairBM;
+      ++n;
+    }
+  }
+  hm[n] = mt;
+  *mtiles = mt;
+  return n;
+}
+
+extern "C" b2_status b2_ep_fused_schedule(int world, int rank, int num_experts, int mode,
+                                          const int32_t *counts, int w2, int32_t *sched,
+                                          int *groups, int *mtiles) {
+  if (world < 1 || world > B2_EP_MAX_WORLD || rank < 0 || rank >= world || !counts || !sched ||
+      !groups || !mtiles)
+    return B2_ERR_INVALID;
+  std::vector<b2_ep_plan> plans(world);
+  for (int q = 0; q < world; ++q)
+    B2_RETURN_IF(b2_ep_plan_compute(world, q, num_experts, mode, counts, &plans[q]));
+  *groups = fill_fused(world, rank, plans.data(), w2 != 0, sched, mtiles);
+  return B2_OK;
+}
+
+// The fused exchange + expert GEMMs (B2_EP_PIPE_FUSED), from the uploaded
+// plan to the moment every source has returned this rank's rows.
+static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
+                             const std::function<b2_status(int)> &tl) {
+  b2_moe *m = ep->moe;
+  const int G = ep->world, r = ep->rank, H = m->d.hidden, Ip = m->Ip;
+  const bool f = m->tf32;
+  const b2_ep_plan &p = ep->plans[r];
+  const size_t rb = (f ? 4 : 2) * (size_t)H;
+  int mt1 = 0, mt2 = 0;
+  const int n1 = fill_fused(G, r, ep->plans.data(), false, ep->h_fsched, &mt1);
+  const int n2 = fill_fused(G, r, ep->plans.data(), true, ep->h_fsched + kFusedSchedInts, &mt2);
+  B2_CUDA(cudaMemcpyAsync(ep->d_fsched, ep->h_fsched, sizeof(int32_t) * 2 * kFusedSchedInts,
+                          cudaMemcpyHostToDevice, s));
+  B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+  int nwait_ret = 0;
+  for (int d = 0; d < G; ++d)
+    if (d != r && p.send_cnt[d] > 0) ep->h_wait_idx[G + nwait_ret++] = kFlagReturn * G + d;
+  if (nwait_ret > 0)
+    B2_CUDA(cudaMemcpyAsync(ep->d_wait_idx + G, ep->h_wait_idx + G, sizeof(int) * nwait_ret,
+                            cudaMemcpyHostToDevice, s));
+  B2_CUDA(cudaEventRecord(ep->ev_ready, s));
+  B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
+  prof_mark(m, s);  // expert GEMMs start
+
+  constexpr int N1 = kMaxGroups + 1;
+  const int32_t *d1 = ep->d_fsched, *d2 = ep->d_fsched + kFusedSchedInts;
+  const int max_pairs = m->sms / 2;
+  // every wait of the W1||W3 launch may last as long as a source's flag wait
+  const uint64_t wait_ns = timeout_ns + kWaitTimeoutNs;
+  GemmArgs a1{};
+  a1.counts = d1;
+  a1.offsets = d1 + N1;
+  a1.mtile_offsets = d1 + 2 * N1;
+  a1.group_b = d1 + 3 * N1;
+  a1.a_offsets = d1 + 4 * N1;
+  a1.group_src = d1 + 5 * N1;
+  a1.num_groups = n1;
+  a1.b_rows_per_group = 2 * Ip;
+  a1.N = Ip;
+  a1.num_n_tiles = Ip / 128;
+  a1.num_k_blocks = f ? H / 32 : H / 64;
+  a1.out = ep->inter;
+  a1.ldo = Ip;
+  a1.status = m->status;
+  a1.flags = ep->flags + kFlagDispatch * G;
+  a1.flag_target = ep->seq;
+  a1.c_rows = ep->inter_rows;
+  a1.wait_ns = wait_ns;
+  const int pairs1 = (int)std::min<long long>(max_pairs, (long long)mt1 * a1.num_n_tiles);
+  if (n1 > 0) {
+    if (f)
+      B2_RETURN_IF((launch_gemm_pair<kEpiSwiGLU, true, float>(m->tm_x, m->tm_w13_half, a1, pairs1,
+                                                              s, &ep->tm_recv)));
+    else
+      B2_RETURN_IF((launch_gemm_pair<kEpiSwiGLU, false, __nv_bfloat16>(
+          m->tm_x, m->tm_w13_half, a1, pairs1, s, &ep->tm_recv)));
+  }
+  // dispatch on the copy engine (enqueued after the GEMM, which starts on the
+  // own rows meanwhile): step k pushes the rows for rank r+k into its receive
+  // buffer, then our sequence number into its flag slot
+  const char *sx = reinterpret_cast<const char *>(m->sorted_x);
+  B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_ready, 0));
+  for (int k = 1; k < G; ++k) {
+    const int to = (r + k) % G;
+    if (p.send_cnt[to])
+      B2_CUDA(cudaMemcpyAsync(ep->peer_recv[to] + ep->plans[to].recv_off[r] * rb,
+                              sx + p.send_off[to] * rb, p.send_cnt[to] * rb,
+                              cudaMemcpyDeviceToDevice, ep->st_d));
+    B2_CUDA(cudaMemcpyAsync(ep->peer_flags[to] + kFlagDispatch * G + r, ep->d_seq,
+                            sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_d));
+  }
+  B2_RETURN_IF(tl(B2_EP_TL_W13_DONE));
+  prof_mark(m, s);  // W2 starts
+
+  // the largest sout any destination row may fall in: its source's row count
+  int64_t max_src_rows = 0;
+  for (int q = 0; q < G; ++q) {
+    int64_t rows = 0;
+    for (int e = 0; e < ep->E; ++e) rows += ep->h_cnt_all[(size_t)q * ep->E + e];
+    max_src_rows = std::max(max_src_rows, rows);
+  }
+  GemmArgs a2{};
+  a2.counts = d2;
+  a2.offsets = d2 + N1;
+  a2.mtile_offsets = d2 + 2 * N1;
+  a2.group_b = d2 + 3 * N1;
+  a2.a_offsets = d2 + 4 * N1;
+  a2.group_dst = d2 + 6 * N1;
+  a2.out_ptrs = ep->d_out_ptrs;
+  a2.num_groups = n2;
+  a2.b_rows_per_group = H;
+  a2.N = H;
+  a2.num_n_tiles = (H + kBN - 1) / kBN;
+  a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
+  a2.out = m->sout;
+  a2.ldo = H;
+  a2.status = m->status;
+  a2.c_rows = max_src_rows;
+  const int pairs2 = (int)std::min<long long>(max_pairs, (long long)mt2 * a2.num_n_tiles);
+  if (n2 > 0) {
+    if (f)
+      B2_RETURN_IF(
+          (launch_gemm_pair<kEpiStore, true, float>(ep->tm_inter, m->tm_w2_half, a2, pairs2, s)));
+    else
+      B2_RETURN_IF((launch_gemm_pair<kEpiStore, false, __nv_bfloat16>(ep->tm_inter,
+                                                                      m->tm_w2_half, a2, pairs2,
+                                                                      s)));
+  }
+  B2_RETURN_IF(tl(B2_EP_TL_W2_DONE));
+  if (G > 1) {
+    // this rank's results are in every source's sout: raise our return flag there
+    signal_flags_kernel<<<1, 32 * ((G - 1 + 31) / 32), 0, s>>>(ep->d_ret_flags, G - 1, ep->seq);
+    B2_LAUNCHED();
+  }
+  if (nwait_ret > 0) {
+    wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(
+        ep->flags, ep->d_wait_idx + G, nwait_ret, ep->seq, timeout_ns, m->status);
+    B2_LAUNCHED();
+  }
+  if (G > 1) {
+    // the dispatch copies are done before the next forward rewrites sorted_x
+    B2_CUDA(cudaEventRecord(ep->ev_ret, ep->st_d));
+    B2_CUDA(cudaStreamWaitEvent(s, ep->ev_ret, 0));
+  }
+  B2_RETURN_IF(tl(B2_EP_TL_RETURNED));
+  return B2_OK;
+}
+
 b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaStream_t s,
                              bool accumulate) {
-  if (!ep || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (!ep || T < 0 || (T > 0 && (!x || !y || !aligned16(x) || !aligned16(y))))
+    return B2_ERR_INVALID;
   if (!ep->cm->ok) return B2_ERR_COMM;
   b2_moe *m = ep->moe;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   const int E = ep->E, G = ep->world, r = ep->rank, H = m->d.hidden;
   const size_t rb = (m->tf32 ? 4 : 2) * (size_t)H;  // bytes per row
   const uint64_t timeout_ns = (uint64_t)(ep->timeout_s * 1e9);
-  auto tl = [&](int tag) -> b2_status {
+  const std::function<b2_status(int)> tl = [&](int tag) -> b2_status {
     if (!m->profile) return B2_OK;
     if (ep->tl_n >= (int)ep->tl_ev.size()) {
       cudaEvent_t e = nullptr;
@@ -666,6 +902,21 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
     B2_RETURN_IF(b2_ep_plan_compute(G, q, E, ep->mode, ep->h_cnt_all, &ep->plans[q]));
   const b2_ep_plan &p = ep->plans[r];
   if (p.recv_rows > ep->cap_rows) return B2_ERR_CAPACITY;
+  ep->seq += 1;
+  *ep->h_seq = ep->seq;
+  if (ep->pipeline == B2_EP_PIPE_FUSED) {
+    B2_RETURN_IF(fused_gemms(ep, s, timeout_ns, tl));
+    // 6. local k-ordered combine
+    if (T > 0) {
+      B2_RETURN_IF(moe_combine_stage(m, y, T, s, accumulate));
+    } else {
+      for (int i = 0; i < 2; ++i) prof_mark(m, s);
+    }
+    ep->host_wait_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+    ep->host_enqueue_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - h1).count();
+    return tl(B2_EP_TL_DONE);
+  }
   // schedule slots: one per source; the rank's own rows are split in two
   // (slot r before the remote steps, slot G after them) so that the return of
   // the last remote step overlaps the second half
@@ -682,8 +933,6 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   int nwait_ret = 0;
   for (int d = 0; d < G; ++d)
     if (d != r && p.send_cnt[d] > 0) ep->h_wait_idx[G + nwait_ret++] = kFlagReturn * G + d;
-  ep->seq += 1;
-  *ep->h_seq = ep->seq;
   B2_CUDA(cudaMemcpyAsync(ep->d_sched, ep->h_sched, sizeof(int32_t) * kSchedInts * (G + 1),
                           cudaMemcpyHostToDevice, s));
   B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
@@ -799,6 +1048,13 @@ extern "C" b2_status b2_ep_profile_timeline(b2_ep *ep, int max, int *tags, float
     ms[k++] = (float)ep->host_enqueue_ms;
   }
   *n = k;
+  return B2_OK;
+}
+
+extern "C" b2_status b2_ep_set_pipeline(b2_ep *ep, int pipeline) {
+  if (!ep || (pipeline != B2_EP_PIPE_FUSED && pipeline != B2_EP_PIPE_STAGED))
+    return B2_ERR_INVALID;
+  ep->pipeline = pipeline;
   return B2_OK;
 }
 

@@ -63,6 +63,17 @@ struct GemmArgs {
   long long ldo;             // output row stride in elements
   int *status;
   int accumulate;            // fp32 output only: C += A . B^T (the residual add, fused)
+  // ---- expert-parallel extensions of the grouped CTA-pair schedule (all
+  // optional; zero / null keeps the plain grouped GEMM):
+  const int *a_offsets;      // first A row of each group when it differs from its C row
+  const int *group_src;      // -1: A rows in tmA now; s >= 0: A rows in tmA2, published
+                             // when flags[s] >= flag_target (a peer's copy engine)
+  const uint64_t *flags;
+  uint64_t flag_target;
+  void *const *out_ptrs;     // output base of each destination (this GPU's or a peer's)
+  const int *group_dst;      // destination of each group (index into out_ptrs)
+  long long c_rows;          // rows of every output buffer (> 0: rows beyond are refused)
+  uint64_t wait_ns;          // bound of every wait of the kernel (0: kWaitTimeoutNs)
 };
 
 // Ring depth for an N-tile width: 192 KB of A+B stages (4 at 256, 6 at 128,
@@ -76,6 +87,9 @@ constexpr size_t gemm_smem_bytes(int bn = kBN) {
 
 struct TileInfo {
   int a_row, b_row, rows_valid, n_tile, cols_valid;
+  int c_row;  // first output row (= a_row unless the group has its own A offset)
+  int src;    // -1, or the peer whose flag publishes the A rows
+  int dst;    // output destination (index into GemmArgs::out_ptrs)
 };
 
 __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
@@ -112,6 +126,9 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
     t.n_tile = n;
   }
   t.cols_valid = min(out_tile_cols, g.N - t.n_tile * out_tile_cols);
+  t.c_row = t.a_row;
+  t.src = -1;
+  t.dst = 0;
   return t;
 }
 

@@ -17,6 +17,15 @@
 //   tfull[a]   one per CTA; the leader commits the last k-block's MMAs to both;
 //   tempty[a]  leader's barrier; one arrival per epilogue warp of both CTAs.
 // The grouped schedule's m-tiles are 256 rows (mtile_offsets in 256-row units).
+//
+// Expert-parallel form (GemmArgs' optional fields; ep.cu): one launch covers a
+// rank's own rows and every source rank's rows.  A group may read its A rows
+// from a second tensor map (the receive buffer) once that source's arrival
+// flag reaches the forward's sequence number -- the producer waits on it,
+// bounded, before its first load of the group's rows -- and may store its
+// output rows into another destination (a peer's buffer mapped over NVLink),
+// so the exchange overlaps the GEMM tile by tile instead of splitting it into
+// one launch per source.
 #pragma once
 #include "gemm_sm100.cuh"
 
@@ -26,18 +35,24 @@ constexpr int kPairBM = 256;  // rows per CTA-pair tile (128 per CTA)
 constexpr int kPairStages = 6;
 constexpr int kPairABytes = 128 * kBKBytes;  // 16 KB
 constexpr int kPairBBytes = 128 * kBKBytes;  // 16 KB: half of the 256-wide B tile
+// per-group schedule arrays in shared memory: m-tile prefix, C offset, count,
+// B block, A offset, source, destination
+constexpr int kPairSchedArrays = 7;
 
 constexpr size_t gemm_pair_smem_bytes() {
   return 1024 + (size_t)kPairStages * (kPairABytes + kPairBBytes) + kEpiStageBytes + 512 +
-         4 * (kMaxGroups + 1) * 4;
+         kPairSchedArrays * (kMaxGroups + 1) * 4;
 }
 
 __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g, const int *s_mt,
                                                      const int *s_off, const int *s_cnt,
-                                                     const int *s_grp, int out_tile_cols,
-                                                     int crank) {
+                                                     const int *s_grp, const int *s_aoff,
+                                                     const int *s_src, const int *s_dst,
+                                                     int out_tile_cols, int crank) {
   TileInfo t;
   const int NT = g.num_n_tiles;
+  t.src = -1;
+  t.dst = 0;
   if (g.num_groups > 0) {
     const int gm = tile / NT;
     const int n = tile - gm * NT;
@@ -47,10 +62,14 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
       if (s_mt[mid] <= gm) lo = mid; else hi = mid;
     }
     const int m = gm - s_mt[lo];
-    t.a_row = s_off[lo] + m * kPairBM + 128 * crank;
-    t.rows_valid = min(128, s_cnt[lo] - m * kPairBM - 128 * crank);
+    const int within = m * kPairBM + 128 * crank;
+    t.c_row = s_off[lo] + within;
+    t.a_row = (g.a_offsets ? s_aoff[lo] : s_off[lo]) + within;
+    t.rows_valid = min(128, s_cnt[lo] - within);
     t.b_row = s_grp[lo] * g.b_rows_per_group + n * kBN + 128 * crank;
     t.n_tile = n;
+    if (g.group_src) t.src = s_src[lo];
+    if (g.group_dst) t.dst = s_dst[lo];
   } else {
     const int MT = (g.M + kPairBM - 1) / kPairBM;
     const int band = g.group_m * NT;
@@ -61,6 +80,7 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
     const int n = idx / gh;
     const int m = m0 + (idx - n * gh);
     t.a_row = m * kPairBM + 128 * crank;
+    t.c_row = t.a_row;
     t.rows_valid = min(128, g.M - t.a_row);
     t.b_row = n * kBN + 128 * crank;
     t.n_tile = n;
@@ -72,7 +92,8 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
 template <int EPI, bool TF32, typename TOut>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmA2, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -87,6 +108,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int *s_off = s_mt + (kMaxGroups + 1);
   int *s_cnt = s_off + (kMaxGroups + 1);
   int *s_grp = s_cnt + (kMaxGroups + 1);
+  int *s_aoff = s_grp + (kMaxGroups + 1);
+  int *s_src = s_aoff + (kMaxGroups + 1);
+  int *s_dst = s_src + (kMaxGroups + 1);
+  const uint64_t wait_ns = g.wait_ns ? g.wait_ns : kWaitTimeoutNs;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,6 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (g.group_src) tma_prefetch_desc(&tmA2);
   }
   cluster_sync();  // both CTAs' barriers exist before any remote arrive
   if (warp == 1) {
@@ -127,6 +153,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         s_off[i] = g.offsets[i];
         s_cnt[i] = g.counts[i];
         s_grp[i] = g.group_b ? g.group_b[i] : i;
+        if (g.a_offsets) s_aoff[i] = g.a_offsets[i];
+        if (g.group_src) s_src[i] = g.group_src[i];
+        if (g.group_dst) s_dst[i] = g.group_dst[i];
       }
     }
   }
@@ -150,13 +179,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, last_par = 0;
+      uint64_t arrived = 0;  // sources whose rows this producer has seen published
       for (int tile = pair; tile < total_tiles; tile += npairs) {
-        const TileInfo t =
-            decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols, (int)crank);
+        const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
+                                            s_dst, out_tile_cols, (int)crank);
+        const CUtensorMap *ta = &tmA;
+        if (t.src >= 0) {
+          ta = &tmA2;
+          if (!((arrived >> (t.src & 63)) & 1)) {
+            if (!flag_wait_ge(g.flags + t.src, g.flag_target, abort_flag, g.status, wait_ns))
+              break;
+            fence_proxy_async_global();  // the rows the flag published, for the TMA loads
+            arrived |= 1ull << (t.src & 63);
+          }
+        }
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, g.status,
-                         kDevTimeoutProducer)) {
+                         kDevTimeoutProducer, wait_ns)) {
             ok = false;
             break;
           }
@@ -166,7 +206,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           else
             mbar_arrive_cluster(lead_full);
           const int kc = kb * (TF32 ? 32 : 64);
-          tma_load_2d_pair(smem_u32(sA + stage * kPairABytes), &tmA, lead_full, kc, t.a_row, pol);
+          tma_load_2d_pair(smem_u32(sA + stage * kPairABytes), ta, lead_full, kc, t.a_row, pol);
           tma_load_2d_pair(smem_u32(sB + stage * kPairBBytes), &tmB, lead_full, kc, t.b_row, pol);
           issued |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
@@ -196,13 +236,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t acc_par = 0;
       bool issued_any = false;
       for (int tile = pair; tile < total_tiles; tile += npairs) {
-        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1, abort_flag, g.status, kDevTimeoutMma))
+        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1, abort_flag, g.status, kDevTimeoutMma,
+                       wait_ns))
           break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * kBN);
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag, g.status, kDevTimeoutMma)) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, g.status, kDevTimeoutMma, wait_ns)) {
             ok = false;
             break;
           }
@@ -243,13 +284,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_par = 0;
     for (int tile = pair; tile < total_tiles; tile += npairs) {
-      const TileInfo t =
-          decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, out_tile_cols, (int)crank);
-      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue)) break;
+      const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
+                                          s_dst, out_tile_cols, (int)crank);
+      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue,
+                     wait_ns))
+        break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
-      const int rows_valid = t.rows_valid - q * 32;  // of this warp's 32 rows
-      TOut *out = reinterpret_cast<TOut *>(g.out) + (long long)(t.a_row + q * 32) * g.ldo +
+      int rows_valid = t.rows_valid - q * 32;  // of this warp's 32 rows
+      // an output row outside the destination buffer (a corrupt schedule) is
+      // refused and recorded instead of written
+      if (g.c_rows > 0 && rows_valid > 0 &&
+          (t.c_row < 0 || (long long)t.c_row + t.rows_valid > g.c_rows)) {
+        if (lane == 0 && g.status) atomicCAS(g.status, 0, (int)kDevBadSlot);
+        rows_valid = 0;
+      }
+      TOut *obase = reinterpret_cast<TOut *>(g.out_ptrs ? g.out_ptrs[t.dst] : g.out);
+      TOut *out = obase + (long long)(t.c_row + q * 32) * g.ldo +
                   (long long)t.n_tile * out_tile_cols;
       if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll 1

@@ -146,7 +146,8 @@ extern "C" b2_status b2_mlp_forward(b2_mlp *m, const float *x, float *y, int T,
 
 b2_status b2::mlp_forward_impl(b2_mlp *m, const float *x, float *y, int T, cudaStream_t s,
                                bool accumulate) {
-  if (!m || T < 0 || (T > 0 && (!x || !y))) return B2_ERR_INVALID;
+  if (!m || T < 0 || (T > 0 && (!x || !y || !aligned16(x) || !aligned16(y))))
+    return B2_ERR_INVALID;
   if (T > m->d.max_tokens) return B2_ERR_CAPACITY;
   if (T == 0) return B2_OK;
   const int H = m->d.hidden, Ip = m->Ip;

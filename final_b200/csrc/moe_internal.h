@@ -47,6 +47,11 @@ std::atomic<uint64_t> &launch_counter();
     if (s_ != B2_OK) return s_; \
   } while (0)
 
+// 16-byte alignment of a caller's buffer: the kernels read and write x / y
+// rows as 16-byte vectors (cp.async, float4 / uint4), so a misaligned
+// pointer is refused before any launch instead of faulting on the device.
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 struct DevInfo {
   int sms = 0;
   int cc_major = 0;
@@ -111,9 +116,11 @@ b2_status launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
 
 // The same GEMM run by CTA pairs (2-CTA clusters, cta_group::2 UMMA): `pairs`
 // clusters of two CTAs.  The grouped schedule's m-tiles are kPairBM rows.
+// ta2: A operand of the groups GemmArgs::group_src marks as remote (the
+// expert-parallel receive buffer); ta when null.
 template <int EPI, bool TF32, typename TOut>
 b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
-                           int pairs, cudaStream_t s) {
+                           int pairs, cudaStream_t s, const CUtensorMap *ta2 = nullptr) {
   auto kern = gemm_pair_kernel<EPI, TF32, TOut>;
   const size_t smem = gemm_pair_smem_bytes();
   static std::atomic<uint64_t> attr_done{0};  // per template instance = per kernel
@@ -133,7 +140,7 @@ b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const G
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, ta2 ? *ta2 : ta, args));
   B2_LAUNCHED();
   return B2_OK;
 }

@@ -285,12 +285,14 @@ static __global__ void __launch_bounds__(1024)
 }
 
 // ---------------------------------------------------------------------------
-// scatter_kernel: block b handles tokens [16b, 16b+16) with 16*K threads
-// (rounded up to whole warps),
-// thread p owns pair (token 32b + p/K, rank p%K).  Its slot is
+// scatter_kernel: block b handles tokens [32b, 32b+32) (kRouteTB) with 32*K
+// threads (rounded up to whole warps); thread p owns pair (token 32b + p/K,
+// rank p%K).  Its slot is
 //   block_base[b][e] + #{pairs p' < p in this block with the same expert}
 // which is the canonical token-major order of the CPU oracle.  Then the block
 // copies each token row once from fp32 x into its K slots as bf16 (or fp32).
+// An expert id of -1 (no expert selected) is dropped (slot -1); an id outside
+// [-1, E) is dropped the same way and recorded as kDevBadExpert in *status.
 // ---------------------------------------------------------------------------
 __host__ __device__ constexpr int scatter_threads(int K) { return (kRouteTB * K + 31) / 32 * 32; }
 
@@ -314,7 +316,12 @@ __global__ void __launch_bounds__(256)
   int e = -1;
   if (p < npairs && t < T) {
     e = topk_idx[(size_t)t * K + (p % K)];
-    if (e < 0 || e >= E) e = -1;
+    if (e >= E || e < -1) {
+      if (status) atomicCAS(status, 0, (int)kDevBadExpert);
+      e = -1;
+    } else if (e < 0) {
+      e = -1;
+    }
   }
   const unsigned peers = __match_any_sync(0xffffffffu, e);
   const int rank_w = __popc(peers & ((1u << lane) - 1u));
@@ -375,6 +382,31 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// hist_kernel: the per-block expert histogram route_kernel produces, for
+// expert ids the caller computed (b2_moe_dispatch_slots).  One block of 128
+// threads per kRouteTB tokens; ids outside [0, E) are not counted (the
+// scatter drops and records them).
+// ---------------------------------------------------------------------------
+static __global__ void __launch_bounds__(128)
+    hist_kernel(const int *__restrict__ topk_idx, int T, int E, int K,
+                int *__restrict__ block_counts) {
+  __shared__ int hist[kMaxExperts];
+  if (threadIdx.x < kMaxExperts) hist[threadIdx.x] = 0;
+  pdl_wait();
+  pdl_trigger();
+  __syncthreads();
+  const int t0 = blockIdx.x * kRouteTB;
+  const int n = min(kRouteTB, T - t0) * K;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = topk_idx[(size_t)t0 * K + i];
+    if (e >= 0 && e < E) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < kMaxExperts)
+    block_counts[(size_t)blockIdx.x * kMaxExperts + threadIdx.x] = hist[threadIdx.x];
 }
 
 // ---------------------------------------------------------------------------

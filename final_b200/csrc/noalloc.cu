@@ -52,7 +52,9 @@ std::mutex g_setup_mu;
 void *g_scratch_ptr[kMaxDevices] = {};
 
 // First call on a device (with that device current): look up the device
-// address of g_route_scratch.  Returns nullptr on failure.
+// address of g_route_scratch.  Returns nullptr on failure.  The address is
+// cached for the life of the process: a cudaDeviceReset unloads the module
+// and invalidates it (documented in include/b2moe.h).
 unsigned char *scratch_for_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -82,6 +84,8 @@ extern "C" b2_status b2_moe_route_noalloc(const float *x, const float *gate, con
       K > E || !gate || (T > 0 && (!x || !topk_idx || !topk_w || !token_slot)) || !counts ||
       !offsets)
     return B2_ERR_INVALID;
+  // route_kernel reads x rows in 16-byte cp.async pieces
+  if (T > 0 && (reinterpret_cast<uintptr_t>(x) & 15)) return B2_ERR_INVALID;
   if (T > kNoAllocMaxTokens || H > kNoAllocMaxHidden) {
     fprintf(stderr,
             "[b2moe] b2_moe_route_noalloc: %d tokens x hidden %d exceeds the fixed scratch "

@@ -93,15 +93,53 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // CTA is aborting (flag already raised, or this wait timed out and raised it).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           volatile int *abort_flag, int *status,
-                                          int code) {
+                                          int code, uint64_t timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > timeout_ns) {
       *abort_flag = 1;
       if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------- cross-GPU flags
+// 64-bit load with acquire semantics at system scope: a flag that another
+// GPU's copy engine (or kernel) writes after the data it publishes.
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t *p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's earlier (generic-proxy) observations of global memory
+// before its later asynchronous-proxy accesses (TMA loads of the published
+// data).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until *flag >= target (the flag lives in this GPU's memory and
+// is written by a peer).  On timeout records kDevTimeoutPeer and raises the
+// CTA's abort flag; returns false when the CTA is aborting.
+__device__ __forceinline__ bool flag_wait_ge(const uint64_t *flag, uint64_t target,
+                                             volatile int *abort_flag, int *status,
+                                             uint64_t timeout_ns) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(128);
+    if (ld_acquire_sys(flag) >= target) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > timeout_ns) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, (int)kDevTimeoutPeer);
       return false;
     }
   }

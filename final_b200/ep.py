@@ -38,6 +38,27 @@ def plan(counts, rank: int, mode: str = "balanced") -> dict:
     return p.to_dict(world)
 
 
+def fused_schedule(counts, rank: int, mode: str = "balanced", w2: bool = False) -> dict:
+    """The group list of one fused launch of `rank` (pure host): per group its
+    row count, C row, A row, local expert, source whose flag it waits on (-1:
+    none) and destination rank; plus the 256-row tile prefix."""
+    lib = _lib.load()
+    import numpy as np
+    c = np.ascontiguousarray(np.asarray(counts, dtype=np.int32))
+    world, E = c.shape
+    n1 = _lib.EP_MAX_SEGMENTS + 1
+    buf = np.zeros(7 * n1, dtype=np.int32)
+    g, mt = C.c_int(0), C.c_int(0)
+    check(lib.b2_ep_fused_schedule(world, rank, E, MODES[mode], c.ctypes.data, int(w2),
+                                   buf.ctypes.data, C.byref(g), C.byref(mt)),
+          "b2_ep_fused_schedule")
+    n = g.value
+    a = buf.reshape(7, n1)
+    return {"count": a[0, :n].copy(), "c_row": a[1, :n].copy(), "mtile": a[2, :n + 1].copy(),
+            "expert": a[3, :n].copy(), "a_row": a[4, :n].copy(), "source": a[5, :n].copy(),
+            "dest": a[6, :n].copy(), "mtiles": mt.value}
+
+
 def unique_id() -> bytes:
     lib = _lib.load()
     buf = (C.c_char * 128)()
@@ -55,7 +76,8 @@ class ExpertParallelMoE:
                  *, max_tokens: int, top_k: int = 4, routed_scale: float = 1.0,
                  dtype: str = "bf16", mode: str = "balanced", world: Optional[int] = None,
                  rank: Optional[int] = None, uid: Optional[bytes] = None,
-                 timeout_s: float = 60.0, stream: Optional[torch.cuda.Stream] = None):
+                 timeout_s: float = 60.0, stream: Optional[torch.cuda.Stream] = None,
+                 pipeline: str = "fused"):
         import torch.distributed as dist
         self.lib = _lib.load()
         if world is None:
@@ -93,6 +115,7 @@ class ExpertParallelMoE:
                                     C.byref(handle)), "b2_ep_create")
         self._h = handle
         check(self.lib.b2_ep_set_timeout(self._h, C.c_double(timeout_s)), "b2_ep_set_timeout")
+        self.set_pipeline(pipeline)
 
     def forward_gpu(self, x: torch.Tensor, y: torch.Tensor, num_tokens: int,
                     stream: Optional[torch.cuda.Stream] = None) -> None:
@@ -123,7 +146,16 @@ class ExpertParallelMoE:
         return dict(zip(SparseMoeBlock.STAGES, list(ms))), n.value
 
     TIMELINE = ("start", "scattered", "planned", "own_first", "arrived", "remote_done",
-                "own_second", "returned", "done", "host_wait", "host_enqueue")
+                "own_second", "returned", "done", "host_wait", "host_enqueue", "w13_done",
+                "w2_done")
+    PIPELINES = {"fused": 0, "staged": 1}
+
+    def set_pipeline(self, pipeline: str) -> None:
+        """"fused" (default): one W1||W3 and one W2 launch over every source's
+        rows, results stored into their sources by the W2 epilogue; "staged":
+        a launch pair per source, results returned by the copy engine."""
+        check(self.lib.b2_ep_set_pipeline(self._h, self.PIPELINES[pipeline]),
+              "b2_ep_set_pipeline")
 
     def timeline(self) -> list:
         """[(mark, us since the forward started)] of the last forward run with

@@ -106,17 +106,38 @@ b2_status b2_moe_forward_ex(b2_moe *moe, const float *x, float *y,
  * loading this library holds until exit.
  * x [T,H] f32, gate [E,H] f32, bias [E] f32 or NULL (device pointers);
  * outputs topk_idx/topk_w/token_slot [T,K], counts/offsets [E].
- * Limits: T <= 65536, H <= 4096 (multiple of 64), E <= 32, K <= 8; larger
- * sizes return B2_ERR_CAPACITY.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race and must not be issued. */
+ * Limits: T > 65536 or H > 4096 return B2_ERR_CAPACITY (the fixed scratch is
+ * sized for them); H not a multiple of 64, E outside 1..32, K outside 1..8 or
+ * above E, a NULL required pointer or an x that is not 16-byte aligned
+ * return B2_ERR_INVALID, all before any device work.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.  The
+ * address is kept for the life of the process, so a cudaDeviceReset (which
+ * unloads the module) leaves this entry point unusable on that device.  All
+ * calls share the array: calls that overlap on the GPU race and must not be
+ * issued. */
 b2_status b2_moe_route_noalloc(const float *x, const float *gate,
                                const float *bias, int num_tokens, int hidden,
                                int num_experts, int top_k, float routed_scale,
                                int32_t *topk_idx, float *topk_w,
                                int32_t *counts, int32_t *offsets,
                                int32_t *token_slot, b2_stream stream);
+
+/* Slot bookkeeping of the scatter for expert ids the caller computed itself
+ * (e.g. with a router of its own): per-expert counts and offsets and the
+ * token -> slot map in the canonical token-major order, on the object's
+ * scratch (no allocation).  Replaces moe_scan_kernel and the slot part of
+ * moe_scatter_kernel (src/layer.cu:730-768, 501-542) run on a router's
+ * output.  topk_idx [T,K] i32 and token_slot [T,K] i32 are device pointers,
+ * T <= max_tokens; counts / offsets ([E] i32, device) may be NULL.  An id of
+ * -1 means "no expert" and gets slot -1; an id outside [-1, E) also gets slot
+ * -1 and is recorded as device status 0x201 (read with b2_moe_get_status),
+ * so a corrupt id never addresses memory.  No counterpart of its own in the
+ * reference, whose scatter assumes valid ids (src/layer.cu:515-523). */
+b2_status b2_moe_dispatch_slots(b2_moe *moe, const int32_t *topk_idx,
+                                int num_tokens, int32_t *counts,
+                                int32_t *offsets, int32_t *token_slot,
+                                b2_stream stream);
 
 /* Synchronises `stream`, returns the device status word (0 = ok) in
  * *device_status and clears it.  B2_ERR_DEVICE when it was non-zero. */
@@ -181,6 +202,13 @@ const char *b2_status_string(b2_status s);
 
 /* Library build identification string. */
 const char *b2_version(void);
+
+/* The architecture the library's device code was compiled for, as the CUDA
+ * runtime reports it for one of the library's kernels on the current device
+ * (cudaFuncGetAttributes binaryVersion: major * 10 + minor, 100 for sm_100a).
+ * Needs a device; B2_ERR_CUDA when the kernel cannot be loaded on it.  No
+ * counterpart in the reference. */
+b2_status b2_device_code_version(int *version);
 
 #ifdef __cplusplus
 }

@@ -116,8 +116,49 @@ enum {
   B2_EP_TL_DONE = 8,        /* combine done */
   /* host-side durations of the same forward (ms, not times since the first mark) */
   B2_EP_TL_HOST_WAIT = 9,   /* the host's wait for the count matrix */
-  B2_EP_TL_HOST_ENQUEUE = 10 /* from that wait's end until the forward returned */
+  B2_EP_TL_HOST_ENQUEUE = 10, /* from that wait's end until the forward returned */
+  /* marks of the fused pipeline (B2_EP_PIPE_FUSED) */
+  B2_EP_TL_W13_DONE = 11,   /* the one W1||W3 launch over every source's rows */
+  B2_EP_TL_W2_DONE = 12     /* the one W2 launch, results stored into their sources */
 };
+
+/* How a rank runs its expert GEMMs over the rows of every source. */
+typedef enum b2_ep_pipeline {
+  /* One persistent W1||W3 launch over the rank's own rows and every source's
+   * rows (its TMA producer waits, bounded, on each source's arrival flag
+   * before loading that source's rows) and one W2 launch whose epilogue
+   * stores every row's result straight into the buffer of the rank the row
+   * came from (peer stores over NVLink); a flag per source then tells it the
+   * results are there.  The default. */
+  B2_EP_PIPE_FUSED = 0,
+  /* One W1||W3 + W2 launch pair per source (own rows split around the remote
+   * ones), each remote pair after a flag-wait launch, results returned by
+   * copy-engine writes.  Same results, bit for bit. */
+  B2_EP_PIPE_STAGED = 1
+} b2_ep_pipeline;
+
+/* Selects the pipeline of the following forwards (not collective: every rank
+ * may choose its own; the exchange protocol is the same). */
+b2_status b2_ep_set_pipeline(b2_ep *ep, int pipeline);
+
+/* Number of ints of one fused schedule (b2_ep_fused_schedule). */
+#define B2_EP_FUSED_SCHED_INTS (7 * (B2_EP_MAX_SEGMENTS + 1))
+
+/* Pure host computation (no GPU): the group list one fused launch of `rank`
+ * runs (w2 = 0: W1||W3, w2 != 0: W2), from the [world][E] count matrix (every
+ * rank's plan is derived from it as b2_ep_plan_compute does).  sched receives
+ * B2_EP_FUSED_SCHED_INTS ints: seven arrays of B2_EP_MAX_SEGMENTS + 1 --
+ * row counts, C rows (W1||W3: the receive-layout row of the intermediate; W2:
+ * the row's expert-sorted position at its source), the exclusive prefix of
+ * 256-row tiles (one entry more than groups), local expert index, A rows
+ * (W1||W3: the own rows' expert-sorted position, the receive-layout row for
+ * a peer's rows; W2: the receive-layout row), source rank whose arrival flag
+ * a group waits on (-1: none), destination rank of the results.  *groups and
+ * *mtiles: the list's length and tile count.  No counterpart in the
+ * reference; exposed so the schedule's row mapping is testable on a CPU. */
+b2_status b2_ep_fused_schedule(int world, int rank, int num_experts, int mode,
+                               const int32_t *counts, int w2, int32_t *sched,
+                               int *groups, int *mtiles);
 
 /* Timeline of the last forward run with profiling on (b2_moe_profile_enable
  * on b2_ep_layer(ep)): *n marks (at most max), tags[i] one of B2_EP_TL_*,

@@ -43,3 +43,18 @@ def test_reference_arm_other_ranks_are_silent():
     r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}, "--gpus", "2")
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [l for l in r.stdout.splitlines() if l.startswith("{")]
+
+
+def test_reference_arm_config_is_ours(monkeypatch):
+    """Both arms print the same `config` dict for the same arguments (it is a
+    function of the arguments alone), so the driver can match the lines."""
+    r = _run(None, "--gpus", "2")
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][0])
+    sys.path.insert(0, str(ROOT))
+    import bench
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--steps", "1",
+                                      "--warmup", "3", "--tokens", "256", "--gpus", "2"])
+    args = bench.parse()
+    assert d["config"] == bench.bench_config(args, 2)
+    assert "owner placement" in d["config"]["parallelism"]

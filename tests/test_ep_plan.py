@@ -90,6 +90,59 @@ def test_plan_invariants(mode, world, zipf):
                 assert R / world * 0.5 - 2 <= n <= R / world * 1.5 + 2
 
 
+@pytest.mark.parametrize("mode", ["owner", "balanced"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_fused_schedules_map_every_row_once(mode, world):
+    """The fused pipeline's two launches (b2_ep_fused_schedule): W1||W3 writes
+    every receive-layout row exactly once, reads the own rows at their
+    expert-sorted position and a peer's rows behind that peer's flag, own rows
+    first and the peers in arrival order (r-1, r-2, ...); W2 sends every row's
+    result to the expert-sorted row it came from at its source, so over all
+    ranks each source's sorted rows receive exactly one result each."""
+    rng = np.random.default_rng(100 + world)
+    E = 32
+    for zipf in (False, True):
+        cnt = _random_counts(rng, world, E, zipf).astype(np.int32)
+        cnt[:, 5] = 0
+        plans = [epmod.plan(cnt, r, mode) for r in range(world)]
+        returned = [np.zeros(int(cnt[s].sum()), dtype=np.int32) for s in range(world)]
+        for r, p in enumerate(plans):
+            w13 = epmod.fused_schedule(cnt, r, mode, w2=False)
+            w2 = epmod.fused_schedule(cnt, r, mode, w2=True)
+            tiles = np.concatenate([[0], np.cumsum((w13["count"] + 255) // 256)])
+            assert np.array_equal(w13["mtile"], tiles) and w13["mtiles"] == tiles[-1]
+            cover = np.zeros(p["recv_rows"], dtype=np.int32)
+            order = []
+            for c, crow, arow, src, dst in zip(w13["count"], w13["c_row"], w13["a_row"],
+                                                w13["source"], w13["dest"]):
+                cover[crow:crow + c] += 1
+                within = crow - p["recv_off"][src if src >= 0 else r]
+                if src < 0:   # own rows: read in place from this rank's sorted rows
+                    assert arow == p["send_off"][r] + within
+                else:         # a peer's rows: read from the receive buffer
+                    assert src != r and arow == crow
+                order.append(r if src < 0 else src)
+            assert np.all(cover == 1)
+            # own rows first, then the sources in the order their rows arrive
+            seen = list(dict.fromkeys(order))
+            want = [(r - k) % world for k in range(world)]
+            assert seen == [q for q in want if q in seen]
+            # W2: same groups, results to their sources, own rows last
+            assert sorted(w2["count"].tolist()) == sorted(w13["count"].tolist())
+            assert np.all(w2["source"] == -1)
+            for c, crow, arow, dst in zip(w2["count"], w2["c_row"], w2["a_row"], w2["dest"]):
+                within = arow - p["recv_off"][dst]
+                assert 0 <= within and within + c <= p["recv_cnt"][dst]
+                assert crow == plans[dst]["send_off"][r] + within
+                returned[dst][crow:crow + c] += 1
+            if len(w2["dest"]):
+                dests = list(dict.fromkeys(w2["dest"].tolist()))
+                if r in dests:
+                    assert dests[-1] == r
+        for s in range(world):
+            assert np.all(returned[s] == 1)
+
+
 def test_plan_balanced_removes_zipf_skew():
     rng = np.random.default_rng(0)
     E, world = 32, 8
