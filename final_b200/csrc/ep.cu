@@ -14,9 +14,10 @@
 //      and every source's rows -- the TMA producer of a tile from source s
 //      waits (bounded) on s's arrival flag before loading it, so the GEMM
 //      starts on the own rows at once and takes each source as it lands --
-//      and ONE W2 launch whose epilogue stores each row's result straight into
-//      the sout of the rank the row came from (peer stores over NVLink); a
-//      signal kernel then raises this rank's return flag at every source.
+//      and ONE W2 launch that stores every result locally and counts the
+//      stored tiles per return chunk; the copy engine sends each chunk to its
+//      source as soon as its counter is complete (a stream wait on the
+//      counter), then raises this rank's return flag there.
 //      Staged pipeline: the own rows in place, then per source a bounded flag
 //      wait and a W1||W3 + W2 launch pair, results returned by the copy
 //      engine;
@@ -280,6 +281,15 @@ struct EpComm {
   int refs = 1;
 };
 
+// A return chunk of the fused pipeline: consecutive W2 groups of one source,
+// receive-layout rows [row, row+rows) of out_recv, sent to rows [home,
+// home+rows) of the source's sout once its counter reaches `target`.
+struct ReturnChunk {
+  int src;
+  int64_t row, home, rows;
+  uint64_t target;  // epilogue-warp completions of the chunk's tiles
+};
+
 struct b2_ep {
   b2_moe *moe = nullptr;
   int world = 1, rank = 0, mode = 0, E = 0, n_wexp = 0;
@@ -299,8 +309,12 @@ struct b2_ep {
   CUtensorMap tm_recv, tm_inter;
   int64_t inter_rows = 0;
   int pipeline = B2_EP_PIPE_FUSED;
-  void **d_out_ptrs = nullptr;         // [world]: sout of every rank (own, peers over IPC)
-  uint64_t **d_ret_flags = nullptr;    // [world-1]: our return-flag slot at each peer
+  bool fused_ok = false;               // the device supports the fused pipeline's waits
+  void **d_out_ptrs = nullptr;         // [world]: W2 destination by source rank: this
+                                       // rank -> sout, a peer -> out_recv
+  unsigned long long *d_chunk_done = nullptr;  // [kMaxGroups]: return-chunk counters
+  std::vector<ReturnChunk> chunks;     // return chunks of the last forward
+  cudaEvent_t ev_w2go = nullptr, ev_dsp = nullptr;
   int32_t *d_fsched = nullptr, *h_fsched = nullptr;  // fused schedules: W1||W3, then W2
   int32_t *d_cnt_all = nullptr, *h_cnt_all = nullptr;
   int32_t *d_sched = nullptr, *h_sched = nullptr;  // per source: counts|offsets|mtile|group_b
@@ -317,14 +331,45 @@ static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
 // a fused schedule: counts | C rows | m-tile prefix | expert | A rows | source | destination
 static constexpr int kFusedSchedInts = kPairSchedArrays * (kMaxGroups + 1);
 
-// Raises this rank's flag at every peer once the preceding W2 launch (whose
-// epilogue stored the peers' rows into their sout) has completed: a plain
-// stream-ordered launch, so every store of that grid has been performed
-// before the release stores below.
-static __global__ void signal_flags_kernel(uint64_t *const *flag_ptrs, int n, uint64_t value) {
-  __threadfence_system();
-  const int i = threadIdx.x;
-  if (i < n) st_release_sys(flag_ptrs[i], value);
+// Sets every return-chunk counter far past any target (after W2 on the same
+// stream), so that a copy-engine wait on a counter always ends even if W2
+// aborted before counting all of its tiles.
+static __global__ void release_counters_kernel(unsigned long long *counters, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) counters[i] = 1ull << 62;
+}
+
+// cuStreamWaitValue64 / cuDeviceGetAttribute from the driver, looked up once
+// through the runtime (the library links no driver library).
+typedef CUresult (*WaitValue64Fn)(CUstream, CUdeviceptr, cuuint64_t, unsigned int);
+typedef CUresult (*DevAttrFn)(int *, CUdevice_attribute, CUdevice);
+static WaitValue64Fn ep_wait_value64() {
+  static WaitValue64Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWaitValue64", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<WaitValue64Fn>(p);
+  });
+  return fn;
+}
+// Whether the current device can wait on 64-bit values in a stream (the
+// fused pipeline's return copies need it).
+static bool stream_wait64_supported() {
+  if (!ep_wait_value64()) return false;
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuDeviceGetAttribute", &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return false;
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (reinterpret_cast<DevAttrFn>(p)(&v, CU_DEVICE_ATTRIBUTE_CAN_USE_64_BIT_STREAM_MEM_OPS,
+                                     (CUdevice)dev) != CUDA_SUCCESS)
+    return false;
+  return v != 0;
 }
 
 // Bounded wait, on this GPU, for flags[idx[i]] >= target (one lane per flag).
@@ -447,6 +492,8 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   if (ep->ev_scan) cudaEventDestroy(ep->ev_scan);
   for (cudaEvent_t e : ep->tl_ev) cudaEventDestroy(e);
   if (ep->ev_cnt) cudaEventDestroy(ep->ev_cnt);
+  if (ep->ev_w2go) cudaEventDestroy(ep->ev_w2go);
+  if (ep->ev_dsp) cudaEventDestroy(ep->ev_dsp);
   if (ep->st_d) cudaStreamDestroy(ep->st_d);
   if (ep->st_r) cudaStreamDestroy(ep->st_r);
   if (ep->h_cnt_all) cudaFreeHost(ep->h_cnt_all);
@@ -517,8 +564,11 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
     return fail(st);
   if ((st = moe_alloc(m, (void **)&ep->d_out_ptrs, sizeof(void *) * world)) != B2_OK)
     return fail(st);
-  if ((st = moe_alloc(m, (void **)&ep->d_ret_flags, sizeof(void *) * world)) != B2_OK)
+  if ((st = moe_alloc(m, (void **)&ep->d_chunk_done, sizeof(unsigned long long) * kMaxGroups)) !=
+      B2_OK)
     return fail(st);
+  ep->fused_ok = stream_wait64_supported();
+  if (!ep->fused_ok) ep->pipeline = B2_EP_PIPE_STAGED;
   if (cudaMallocHost(&ep->h_cnt_all, sizeof(int32_t) * world * kMaxExperts) != cudaSuccess ||
       cudaMallocHost(&ep->h_sched, sizeof(int32_t) * kSchedInts * (world + 1)) != cudaSuccess ||
       cudaMallocHost(&ep->h_seq, sizeof(uint64_t)) != cudaSuccess ||
@@ -537,7 +587,9 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
       cudaEventCreateWithFlags(&ep->ev_ready, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->ev_ret, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->ev_scan, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->ev_cnt, cudaEventDisableTiming) != cudaSuccess)
+      cudaEventCreateWithFlags(&ep->ev_cnt, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_w2go, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_dsp, cudaEventDisableTiming) != cudaSuccess)
     return fail(B2_ERR_CUDA);
   ep->ev_out.resize(world, nullptr);
   for (int k = 0; k < world; ++k)
@@ -603,18 +655,12 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
       ep->peer_flags[p] = static_cast<uint64_t *>(ptr);
     }
   }
-  // output bases of the fused W2 (every rank's sout) and this rank's
-  // return-flag slot at each peer, in exchange-step order
+  // W2 destinations of the fused pipeline, by source rank: this rank's own
+  // rows go to sout, a peer's rows to out_recv (returned by the copy engine)
   {
-    std::vector<void *> outs(world), rets(world, nullptr);
-    for (int p = 0; p < world; ++p) outs[p] = p == rank ? m->sout : ep->peer_sout[p];
-    for (int k = 1; k < world; ++k) {
-      const int from = (rank - k + world) % world;
-      rets[k - 1] = ep->peer_flags[from] + kFlagReturn * world + rank;
-    }
+    std::vector<void *> outs(world);
+    for (int p = 0; p < world; ++p) outs[p] = p == rank ? m->sout : ep->out_recv;
     if (cudaMemcpy(ep->d_out_ptrs, outs.data(), sizeof(void *) * world,
-                   cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(ep->d_ret_flags, rets.data(), sizeof(void *) * world,
                    cudaMemcpyHostToDevice) != cudaSuccess)
       return fail(B2_ERR_CUDA);
   }
@@ -663,39 +709,68 @@ static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self
 // expert-sorted rows, so the GEMM starts at once -- then the sources in the
 // order their rows arrive (rank s pushes to s+1 first, so r-1, r-2, ...), A =
 // the receive buffer behind that source's flag; C = the receive-layout row
-// (inter).  W2 (w2 = true): the remote sources first and the own rows last
-// (their results need no NVLink, so the last stores of the launch stay
-// local); A = the inter row; C = the row's expert-sorted position at its
-// source, destination = the source.  Within a source the groups keep the
-// plan's expert order.  Returns the number of groups; *mtiles the m-tiles.
-static int fill_fused(int G, int r, const b2_ep_plan *plans, bool w2, int32_t *h, int *mtiles) {
+// (inter).  W2 (w2 = true): the remote sources first and the own rows last;
+// A = the inter row; the own rows' results go to sout at their expert-sorted
+// row (destination r), a peer's rows' results to out_recv at their
+// receive-layout row (destination: the peer), grouped into return chunks of
+// consecutive groups of one source (about kReturnChunkRows rows each) that
+// the copy engine sends home as soon as their tiles are stored.  Within a
+// source the groups keep the plan's expert order.  Returns the number of
+// groups; *mtiles the 256-row tiles; `chunks` (may be null) the return chunks
+// with their counter targets for W2's n_tiles output tiles per row block.
+constexpr int64_t kReturnChunkRows = 4096;
+
+static int fill_fused(int G, int r, const b2_ep_plan *plans, bool w2, int n_tiles, int32_t *h,
+                      int *mtiles, std::vector<ReturnChunk> *chunks) {
   constexpr int N1 = kMaxGroups + 1;
   const b2_ep_plan &p = plans[r];
   int32_t *hc = h, *ho = h + N1, *hm = h + 2 * N1, *hg = h + 3 * N1, *ha = h + 4 * N1,
-          *hs = h + 5 * N1, *hd = h + 6 * N1;
-  int n = 0, mt = 0;
+          *hs = h + 5 * N1, *hd = h + 6 * N1, *hk = h + 7 * N1;
+  if (chunks) chunks->clear();
+  int n = 0, mt = 0, nchunk = 0;
   for (int k = 0; k < G; ++k) {
     const int src = w2 ? (k < G - 1 ? (r - 1 - k + 2 * G) % G : r) : (r - k + G) % G;
+    ReturnChunk cur{-1, 0, 0, 0, 0};
     for (int g = 0; g < p.num_segments; ++g) {
       if (p.seg_source[g] != src) continue;
       const int64_t within = p.seg_off[g] - p.recv_off[src];
       const int64_t home = plans[src].send_off[r] + within;  // its row at the source
+      const int tiles = (p.seg_cnt[g] + kPairBM - 1) / kPairBM;
       hc[n] = p.seg_cnt[g];
       hg[n] = p.seg_expert[g];
+      hk[n] = -1;
       if (!w2) {
         ho[n] = p.seg_off[g];
         ha[n] = (int32_t)(src == r ? home : p.seg_off[g]);
         hs[n] = src == r ? -1 : src;
         hd[n] = 0;
       } else {
-        ho[n] = (int32_t)home;
+        ho[n] = (int32_t)(src == r ? home : p.seg_off[g]);
         ha[n] = p.seg_off[g];
         hs[n] = -1;
         hd[n] = src;
+        if (src != r) {
+          // a new chunk when none is open, the open one is full, or the rows
+          // are not contiguous with it
+          if (cur.src < 0 || cur.rows >= kReturnChunkRows || cur.row + cur.rows != p.seg_off[g]) {
+            if (cur.src >= 0) {
+              if (chunks) chunks->push_back(cur);
+              ++nchunk;
+            }
+            cur = ReturnChunk{src, p.seg_off[g], home, 0, 0};
+          }
+          cur.rows += p.seg_cnt[g];
+          cur.target += 8ull * (uint64_t)tiles * (uint64_t)n_tiles;  // 8 epilogue warps per tile
+          hk[n] = nchunk;
+        }
       }
       hm[n] = mt;
-      mt += (p.seg_cnt[g] + kPairBM - 1) / kPairBM;
+      mt += tiles;
       ++n;
+    }
+    if (cur.src >= 0) {
+      if (chunks) chunks->push_back(cur);
+      ++nchunk;
     }
   }
   hm[n] = mt;
@@ -712,7 +787,7 @@ extern "C" b2_status b2_ep_fused_schedule(int world, int rank, int num_experts, 
   std::vector<b2_ep_plan> plans(world);
   for (int q = 0; q < world; ++q)
     B2_RETURN_IF(b2_ep_plan_compute(world, q, num_experts, mode, counts, &plans[q]));
-  *groups = fill_fused(world, rank, plans.data(), w2 != 0, sched, mtiles);
+  *groups = fill_fused(world, rank, plans.data(), w2 != 0, 1, sched, mtiles, nullptr);
   return B2_OK;
 }
 
@@ -725,9 +800,12 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   const bool f = m->tf32;
   const b2_ep_plan &p = ep->plans[r];
   const size_t rb = (f ? 4 : 2) * (size_t)H;
+  const int nt2 = (H + kBN - 1) / kBN;
   int mt1 = 0, mt2 = 0;
-  const int n1 = fill_fused(G, r, ep->plans.data(), false, ep->h_fsched, &mt1);
-  const int n2 = fill_fused(G, r, ep->plans.data(), true, ep->h_fsched + kFusedSchedInts, &mt2);
+  const int n1 = fill_fused(G, r, ep->plans.data(), false, 0, ep->h_fsched, &mt1, nullptr);
+  const int n2 = fill_fused(G, r, ep->plans.data(), true, nt2, ep->h_fsched + kFusedSchedInts,
+                            &mt2, &ep->chunks);
+  const int nchunks = (int)ep->chunks.size();
   B2_CUDA(cudaMemcpyAsync(ep->d_fsched, ep->h_fsched, sizeof(int32_t) * 2 * kFusedSchedInts,
                           cudaMemcpyHostToDevice, s));
   B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
@@ -738,6 +816,11 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
     B2_CUDA(cudaMemcpyAsync(ep->d_wait_idx + G, ep->h_wait_idx + G, sizeof(int) * nwait_ret,
                             cudaMemcpyHostToDevice, s));
   B2_CUDA(cudaEventRecord(ep->ev_ready, s));
+  // every return chunk's counter starts at zero (before W1||W3, so that W1||W3
+  // and W2 follow each other directly and overlap by programmatic launch)
+  if (nchunks > 0)
+    B2_CUDA(cudaMemsetAsync(ep->d_chunk_done, 0, sizeof(unsigned long long) * nchunks, s));
+  B2_CUDA(cudaEventRecord(ep->ev_w2go, s));
   B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
   prof_mark(m, s);  // expert GEMMs start
 
@@ -791,13 +874,7 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   B2_RETURN_IF(tl(B2_EP_TL_W13_DONE));
   prof_mark(m, s);  // W2 starts
 
-  // the largest sout any destination row may fall in: its source's row count
-  int64_t max_src_rows = 0;
-  for (int q = 0; q < G; ++q) {
-    int64_t rows = 0;
-    for (int e = 0; e < ep->E; ++e) rows += ep->h_cnt_all[(size_t)q * ep->E + e];
-    max_src_rows = std::max(max_src_rows, rows);
-  }
+  // W2: own rows into sout, a peer's rows into out_recv (local stores only)
   GemmArgs a2{};
   a2.counts = d2;
   a2.offsets = d2 + N1;
@@ -805,16 +882,20 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   a2.group_b = d2 + 3 * N1;
   a2.a_offsets = d2 + 4 * N1;
   a2.group_dst = d2 + 6 * N1;
+  a2.group_chunk = d2 + 7 * N1;
+  a2.chunk_done = ep->d_chunk_done;
   a2.out_ptrs = ep->d_out_ptrs;
   a2.num_groups = n2;
   a2.b_rows_per_group = H;
   a2.N = H;
-  a2.num_n_tiles = (H + kBN - 1) / kBN;
+  a2.num_n_tiles = nt2;
   a2.num_k_blocks = f ? Ip / 32 : Ip / 64;
   a2.out = m->sout;
   a2.ldo = H;
   a2.status = m->status;
-  a2.c_rows = max_src_rows;
+  // rows of the larger destination: out_recv (a peer's rows, receive layout)
+  // or sout (own rows, expert-sorted)
+  a2.c_rows = std::max<int64_t>(ep->cap_rows, (int64_t)m->d.max_tokens * m->d.top_k);
   const int pairs2 = (int)std::min<long long>(max_pairs, (long long)mt2 * a2.num_n_tiles);
   if (n2 > 0) {
     if (f)
@@ -825,11 +906,38 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
                                                                       m->tm_w2_half, a2, pairs2,
                                                                       s)));
   }
-  B2_RETURN_IF(tl(B2_EP_TL_W2_DONE));
-  if (G > 1) {
-    // this rank's results are in every source's sout: raise our return flag there
-    signal_flags_kernel<<<1, 32 * ((G - 1 + 31) / 32), 0, s>>>(ep->d_ret_flags, G - 1, ep->seq);
+  if (nchunks > 0) {
+    // once W2 has finished -- normally or by an abort that left tiles
+    // uncounted -- every chunk counter is past its target, so no wait of the
+    // return stream below can outlive this forward's kernels
+    release_counters_kernel<<<1, 256, 0, s>>>(ep->d_chunk_done, nchunks);
     B2_LAUNCHED();
+  }
+  B2_RETURN_IF(tl(B2_EP_TL_W2_DONE));
+
+  // return: each chunk goes home on the copy engine as soon as its counter
+  // says its rows are stored; a source's flag follows its last chunk
+  const char *ro = reinterpret_cast<const char *>(ep->out_recv);
+  B2_CUDA(cudaStreamWaitEvent(ep->st_r, ep->ev_w2go, 0));
+  for (int d = 0; d < G; ++d) {  // sources without rows here: nothing to wait for
+    if (d == r || p.recv_cnt[d] > 0) continue;
+    B2_CUDA(cudaMemcpyAsync(ep->peer_flags[d] + kFlagReturn * G + r, ep->d_seq, sizeof(uint64_t),
+                            cudaMemcpyDeviceToDevice, ep->st_r));
+  }
+  for (int c = 0; c < nchunks; ++c) {
+    const ReturnChunk &ch = ep->chunks[c];
+    CUresult cr = ep_wait_value64()(reinterpret_cast<CUstream>(ep->st_r),
+                                     reinterpret_cast<CUdeviceptr>(ep->d_chunk_done + c),
+                                     ch.target, CU_STREAM_WAIT_VALUE_GEQ);
+    if (cr != CUDA_SUCCESS) {
+      fprintf(stderr, "[b2moe] cuStreamWaitValue64 failed (%d)\n", (int)cr);
+      return B2_ERR_CUDA;
+    }
+    B2_CUDA(cudaMemcpyAsync(ep->peer_sout[ch.src] + ch.home * rb, ro + ch.row * rb, ch.rows * rb,
+                            cudaMemcpyDeviceToDevice, ep->st_r));
+    if (c + 1 == nchunks || ep->chunks[c + 1].src != ch.src)
+      B2_CUDA(cudaMemcpyAsync(ep->peer_flags[ch.src] + kFlagReturn * G + r, ep->d_seq,
+                              sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_r));
   }
   if (nwait_ret > 0) {
     wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(
@@ -837,9 +945,12 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
     B2_LAUNCHED();
   }
   if (G > 1) {
-    // the dispatch copies are done before the next forward rewrites sorted_x
-    B2_CUDA(cudaEventRecord(ep->ev_ret, ep->st_d));
+    // the copy streams are done before the next forward rewrites sorted_x,
+    // out_recv or the chunk counters
+    B2_CUDA(cudaEventRecord(ep->ev_ret, ep->st_r));
     B2_CUDA(cudaStreamWaitEvent(s, ep->ev_ret, 0));
+    B2_CUDA(cudaEventRecord(ep->ev_dsp, ep->st_d));
+    B2_CUDA(cudaStreamWaitEvent(s, ep->ev_dsp, 0));
   }
   B2_RETURN_IF(tl(B2_EP_TL_RETURNED));
   return B2_OK;
@@ -904,7 +1015,7 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   if (p.recv_rows > ep->cap_rows) return B2_ERR_CAPACITY;
   ep->seq += 1;
   *ep->h_seq = ep->seq;
-  if (ep->pipeline == B2_EP_PIPE_FUSED) {
+  if (ep->pipeline == B2_EP_PIPE_FUSED && ep->fused_ok) {
     B2_RETURN_IF(fused_gemms(ep, s, timeout_ns, tl));
     // 6. local k-ordered combine
     if (T > 0) {
@@ -1054,6 +1165,11 @@ extern "C" b2_status b2_ep_profile_timeline(b2_ep *ep, int max, int *tags, float
 extern "C" b2_status b2_ep_set_pipeline(b2_ep *ep, int pipeline) {
   if (!ep || (pipeline != B2_EP_PIPE_FUSED && pipeline != B2_EP_PIPE_STAGED))
     return B2_ERR_INVALID;
+  if (pipeline == B2_EP_PIPE_FUSED && !ep->fused_ok) {
+    fprintf(stderr, "[b2moe] the fused pipeline needs 64-bit stream waits, which this device "
+                    "does not offer\n");
+    return B2_ERR_NO_DEVICE;
+  }
   ep->pipeline = pipeline;
   return B2_OK;
 }

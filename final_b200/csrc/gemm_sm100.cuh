@@ -70,9 +70,12 @@ struct GemmArgs {
                              // when flags[s] >= flag_target (a peer's copy engine)
   const uint64_t *flags;
   uint64_t flag_target;
-  void *const *out_ptrs;     // output base of each destination (this GPU's or a peer's)
+  void *const *out_ptrs;     // output base of each destination (this GPU's buffers)
   const int *group_dst;      // destination of each group (index into out_ptrs)
   long long c_rows;          // rows of every output buffer (> 0: rows beyond are refused)
+  const int *group_chunk;    // return chunk of each group (-1: none) ...
+  unsigned long long *chunk_done;  // ... whose counter every epilogue warp bumps (after
+                             // a fence) once its rows of a tile are stored
   uint64_t wait_ns;          // bound of every wait of the kernel (0: kWaitTimeoutNs)
 };
 
@@ -90,6 +93,7 @@ struct TileInfo {
   int c_row;  // first output row (= a_row unless the group has its own A offset)
   int src;    // -1, or the peer whose flag publishes the A rows
   int dst;    // output destination (index into GemmArgs::out_ptrs)
+  int chunk;  // return chunk of the group (-1: none)
 };
 
 __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
@@ -129,6 +133,7 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmArgs &g,
   t.c_row = t.a_row;
   t.src = -1;
   t.dst = 0;
+  t.chunk = -1;
   return t;
 }
 

@@ -22,10 +22,12 @@
 // rank's own rows and every source rank's rows.  A group may read its A rows
 // from a second tensor map (the receive buffer) once that source's arrival
 // flag reaches the forward's sequence number -- the producer waits on it,
-// bounded, before its first load of the group's rows -- and may store its
-// output rows into another destination (a peer's buffer mapped over NVLink),
-// so the exchange overlaps the GEMM tile by tile instead of splitting it into
-// one launch per source.
+// bounded, before its first load of the group's rows -- may store its output
+// rows into another of this GPU's buffers, and may belong to a return chunk
+// whose completion counter each epilogue warp bumps once its rows of a tile
+// are stored, so the copy engine returns the chunk to its source while the
+// launch continues: the exchange overlaps the GEMM instead of splitting it
+// into one launch per source.
 #pragma once
 #include "gemm_sm100.cuh"
 
@@ -36,8 +38,8 @@ constexpr int kPairStages = 6;
 constexpr int kPairABytes = 128 * kBKBytes;  // 16 KB
 constexpr int kPairBBytes = 128 * kBKBytes;  // 16 KB: half of the 256-wide B tile
 // per-group schedule arrays in shared memory: m-tile prefix, C offset, count,
-// B block, A offset, source, destination
-constexpr int kPairSchedArrays = 7;
+// B block, A offset, source, destination, return chunk
+constexpr int kPairSchedArrays = 8;
 
 constexpr size_t gemm_pair_smem_bytes() {
   return 1024 + (size_t)kPairStages * (kPairABytes + kPairBBytes) + kEpiStageBytes + 512 +
@@ -48,11 +50,13 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
                                                      const int *s_off, const int *s_cnt,
                                                      const int *s_grp, const int *s_aoff,
                                                      const int *s_src, const int *s_dst,
-                                                     int out_tile_cols, int crank) {
+                                                     const int *s_chunk, int out_tile_cols,
+                                                     int crank) {
   TileInfo t;
   const int NT = g.num_n_tiles;
   t.src = -1;
   t.dst = 0;
+  t.chunk = -1;
   if (g.num_groups > 0) {
     const int gm = tile / NT;
     const int n = tile - gm * NT;
@@ -70,6 +74,7 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
     t.n_tile = n;
     if (g.group_src) t.src = s_src[lo];
     if (g.group_dst) t.dst = s_dst[lo];
+    if (g.group_chunk) t.chunk = s_chunk[lo];
   } else {
     const int MT = (g.M + kPairBM - 1) / kPairBM;
     const int band = g.group_m * NT;
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int *s_aoff = s_grp + (kMaxGroups + 1);
   int *s_src = s_aoff + (kMaxGroups + 1);
   int *s_dst = s_src + (kMaxGroups + 1);
+  int *s_chunk = s_dst + (kMaxGroups + 1);
   const uint64_t wait_ns = g.wait_ns ? g.wait_ns : kWaitTimeoutNs;
 
   const int warp = threadIdx.x >> 5;
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (g.a_offsets) s_aoff[i] = g.a_offsets[i];
         if (g.group_src) s_src[i] = g.group_src[i];
         if (g.group_dst) s_dst[i] = g.group_dst[i];
+        if (g.group_chunk) s_chunk[i] = g.group_chunk[i];
       }
     }
   }
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint64_t arrived = 0;  // sources whose rows this producer has seen published
       for (int tile = pair; tile < total_tiles; tile += npairs) {
         const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
-                                            s_dst, out_tile_cols, (int)crank);
+                                            s_dst, s_chunk, out_tile_cols, (int)crank);
         const CUtensorMap *ta = &tmA;
         if (t.src >= 0) {
           ta = &tmA2;
@@ -285,7 +292,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_par = 0;
     for (int tile = pair; tile < total_tiles; tile += npairs) {
       const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
-                                          s_dst, out_tile_cols, (int)crank);
+                                          s_dst, s_chunk, out_tile_cols, (int)crank);
       if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue,
                      wait_ns))
         break;
@@ -332,6 +339,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
+      if (t.chunk >= 0) {
+        // this warp's rows of the tile are stored: count it for the chunk's
+        // return copy (fence first, so the copy engine that waits on the
+        // counter reads the stored rows)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(g.chunk_done + t.chunk, 1ull);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
       acc ^= 1;

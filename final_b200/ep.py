@@ -41,22 +41,23 @@ def plan(counts, rank: int, mode: str = "balanced") -> dict:
 def fused_schedule(counts, rank: int, mode: str = "balanced", w2: bool = False) -> dict:
     """The group list of one fused launch of `rank` (pure host): per group its
     row count, C row, A row, local expert, source whose flag it waits on (-1:
-    none) and destination rank; plus the 256-row tile prefix."""
+    none), the rank its rows came from and (W2) its return chunk; plus the
+    256-row tile prefix."""
     lib = _lib.load()
     import numpy as np
     c = np.ascontiguousarray(np.asarray(counts, dtype=np.int32))
     world, E = c.shape
     n1 = _lib.EP_MAX_SEGMENTS + 1
-    buf = np.zeros(7 * n1, dtype=np.int32)
+    buf = np.zeros(8 * n1, dtype=np.int32)
     g, mt = C.c_int(0), C.c_int(0)
     check(lib.b2_ep_fused_schedule(world, rank, E, MODES[mode], c.ctypes.data, int(w2),
                                    buf.ctypes.data, C.byref(g), C.byref(mt)),
           "b2_ep_fused_schedule")
     n = g.value
-    a = buf.reshape(7, n1)
+    a = buf.reshape(8, n1)
     return {"count": a[0, :n].copy(), "c_row": a[1, :n].copy(), "mtile": a[2, :n + 1].copy(),
             "expert": a[3, :n].copy(), "a_row": a[4, :n].copy(), "source": a[5, :n].copy(),
-            "dest": a[6, :n].copy(), "mtiles": mt.value}
+            "dest": a[6, :n].copy(), "chunk": a[7, :n].copy(), "mtiles": mt.value}
 
 
 def unique_id() -> bytes:
@@ -152,8 +153,9 @@ class ExpertParallelMoE:
 
     def set_pipeline(self, pipeline: str) -> None:
         """"fused" (default): one W1||W3 and one W2 launch over every source's
-        rows, results stored into their sources by the W2 epilogue; "staged":
-        a launch pair per source, results returned by the copy engine."""
+        rows, results returned chunk by chunk by the copy engine as W2 counts
+        them stored; "staged": a launch pair per source, results returned by
+        the copy engine after each pair."""
         check(self.lib.b2_ep_set_pipeline(self._h, self.PIPELINES[pipeline]),
               "b2_ep_set_pipeline")
 

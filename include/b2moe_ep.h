@@ -84,10 +84,11 @@ b2_status b2_ep_create(const b2_moe_desc *desc, int world, int rank,
  * B2_ERR_COMM if a peer does not answer within the timeout (the communicator
  * is then aborted).  Rows for rank r+k are pushed by the copy engine into that
  * rank's receive buffer followed by a sequence-number flag; each rank runs its
- * own rows through the expert GEMMs in place while rows travel, then each
- * source's rows after a bounded wait on its flag (a wait that runs out records
- * a device error readable with b2_moe_get_status on b2_ep_layer), and pushes
- * the results back the same way. */
+ * own rows through the expert GEMMs while rows travel, then each source's rows
+ * after a bounded wait on its flag (a wait that runs out records a device
+ * error readable with b2_moe_get_status on b2_ep_layer) -- in one launch per
+ * projection (B2_EP_PIPE_FUSED) or one launch pair per source
+ * (B2_EP_PIPE_STAGED) -- and pushes the results back the same way. */
 b2_status b2_ep_forward(b2_ep *ep, const float *x, float *y, int num_tokens,
                         b2_stream stream);
 
@@ -119,17 +120,19 @@ enum {
   B2_EP_TL_HOST_ENQUEUE = 10, /* from that wait's end until the forward returned */
   /* marks of the fused pipeline (B2_EP_PIPE_FUSED) */
   B2_EP_TL_W13_DONE = 11,   /* the one W1||W3 launch over every source's rows */
-  B2_EP_TL_W2_DONE = 12     /* the one W2 launch, results stored into their sources */
+  B2_EP_TL_W2_DONE = 12     /* the one W2 launch (its chunks' return copies run meanwhile) */
 };
 
 /* How a rank runs its expert GEMMs over the rows of every source. */
 typedef enum b2_ep_pipeline {
   /* One persistent W1||W3 launch over the rank's own rows and every source's
    * rows (its TMA producer waits, bounded, on each source's arrival flag
-   * before loading that source's rows) and one W2 launch whose epilogue
-   * stores every row's result straight into the buffer of the rank the row
-   * came from (peer stores over NVLink); a flag per source then tells it the
-   * results are there.  The default. */
+   * before loading that source's rows) and one W2 launch over all of them;
+   * W2's epilogue counts every stored tile per return chunk (consecutive rows
+   * of one source), and the copy engine sends each chunk back to its source
+   * as soon as its counter is complete (a 64-bit stream wait on the counter),
+   * then raises this rank's flag there.  The default where the device offers
+   * 64-bit stream waits. */
   B2_EP_PIPE_FUSED = 0,
   /* One W1||W3 + W2 launch pair per source (own rows split around the remote
    * ones), each remote pair after a flag-wait launch, results returned by
@@ -138,24 +141,28 @@ typedef enum b2_ep_pipeline {
 } b2_ep_pipeline;
 
 /* Selects the pipeline of the following forwards (not collective: every rank
- * may choose its own; the exchange protocol is the same). */
+ * may choose its own; the exchange protocol is the same).  B2_ERR_NO_DEVICE
+ * for B2_EP_PIPE_FUSED on a device without 64-bit stream waits. */
 b2_status b2_ep_set_pipeline(b2_ep *ep, int pipeline);
 
 /* Number of ints of one fused schedule (b2_ep_fused_schedule). */
-#define B2_EP_FUSED_SCHED_INTS (7 * (B2_EP_MAX_SEGMENTS + 1))
+#define B2_EP_FUSED_SCHED_INTS (8 * (B2_EP_MAX_SEGMENTS + 1))
 
 /* Pure host computation (no GPU): the group list one fused launch of `rank`
  * runs (w2 = 0: W1||W3, w2 != 0: W2), from the [world][E] count matrix (every
  * rank's plan is derived from it as b2_ep_plan_compute does).  sched receives
- * B2_EP_FUSED_SCHED_INTS ints: seven arrays of B2_EP_MAX_SEGMENTS + 1 --
- * row counts, C rows (W1||W3: the receive-layout row of the intermediate; W2:
- * the row's expert-sorted position at its source), the exclusive prefix of
- * 256-row tiles (one entry more than groups), local expert index, A rows
- * (W1||W3: the own rows' expert-sorted position, the receive-layout row for
- * a peer's rows; W2: the receive-layout row), source rank whose arrival flag
- * a group waits on (-1: none), destination rank of the results.  *groups and
- * *mtiles: the list's length and tile count.  No counterpart in the
- * reference; exposed so the schedule's row mapping is testable on a CPU. */
+ * B2_EP_FUSED_SCHED_INTS ints: eight arrays of B2_EP_MAX_SEGMENTS + 1 --
+ * row counts; C rows (W1||W3: the receive-layout row of the intermediate;
+ * W2: the expert-sorted row in this rank's sout for its own rows, the
+ * receive-layout row of the results buffer for a peer's rows); the exclusive
+ * prefix of 256-row tiles (one entry more than groups); local expert index;
+ * A rows (W1||W3: the own rows' expert-sorted position, the receive-layout
+ * row for a peer's rows; W2: the receive-layout row); source rank whose
+ * arrival flag a group waits on (-1: none); rank the rows came from; W2's
+ * return chunk (-1: none; a chunk is consecutive receive-layout rows of one
+ * source, returned to that source's sout in one copy).  *groups and *mtiles:
+ * the list's length and tile count.  No counterpart in the reference;
+ * exposed so the schedule's row mapping is testable on a CPU. */
 b2_status b2_ep_fused_schedule(int world, int rank, int num_experts, int mode,
                                const int32_t *counts, int w2, int32_t *sched,
                                int *groups, int *mtiles);

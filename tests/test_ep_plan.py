@@ -96,8 +96,9 @@ def test_fused_schedules_map_every_row_once(mode, world):
     """The fused pipeline's two launches (b2_ep_fused_schedule): W1||W3 writes
     every receive-layout row exactly once, reads the own rows at their
     expert-sorted position and a peer's rows behind that peer's flag, own rows
-    first and the peers in arrival order (r-1, r-2, ...); W2 sends every row's
-    result to the expert-sorted row it came from at its source, so over all
+    first and the peers in arrival order (r-1, r-2, ...); W2's results reach
+    the expert-sorted row they came from at their source (own rows directly,
+    a peer's rows through a return chunk of consecutive rows), so over all
     ranks each source's sorted rows receive exactly one result each."""
     rng = np.random.default_rng(100 + world)
     E = 32
@@ -127,14 +128,33 @@ def test_fused_schedules_map_every_row_once(mode, world):
             seen = list(dict.fromkeys(order))
             want = [(r - k) % world for k in range(world)]
             assert seen == [q for q in want if q in seen]
-            # W2: same groups, results to their sources, own rows last
+            # W2: same groups, own rows last; own results straight to sout at
+            # their sorted row, a peer's results to the results buffer at their
+            # receive-layout row, returned in chunks of consecutive rows of one
+            # source to the rows they came from
             assert sorted(w2["count"].tolist()) == sorted(w13["count"].tolist())
             assert np.all(w2["source"] == -1)
-            for c, crow, arow, dst in zip(w2["count"], w2["c_row"], w2["a_row"], w2["dest"]):
+            chunks = {}
+            for c, crow, arow, dst, ch in zip(w2["count"], w2["c_row"], w2["a_row"], w2["dest"],
+                                             w2["chunk"]):
                 within = arow - p["recv_off"][dst]
                 assert 0 <= within and within + c <= p["recv_cnt"][dst]
-                assert crow == plans[dst]["send_off"][r] + within
-                returned[dst][crow:crow + c] += 1
+                if dst == r:
+                    assert ch == -1 and crow == p["send_off"][r] + within
+                    returned[r][crow:crow + c] += 1
+                else:
+                    assert ch >= 0 and crow == arow
+                    chunks.setdefault(int(ch), []).append((int(dst), int(arow), int(c)))
+            assert sorted(chunks) == list(range(len(chunks)))
+            for ch, parts in chunks.items():
+                assert len({d for d, _, _ in parts}) == 1
+                d = parts[0][0]
+                for (_, a0, c0), (_, a1, _) in zip(parts, parts[1:]):
+                    assert a1 == a0 + c0          # consecutive receive-layout rows
+                a0 = parts[0][1]
+                rows = sum(c for _, _, c in parts)
+                home = plans[d]["send_off"][r] + a0 - p["recv_off"][d]
+                returned[d][home:home + rows] += 1
             if len(w2["dest"]):
                 dests = list(dict.fromkeys(w2["dest"].tolist()))
                 if r in dests:
