@@ -13,7 +13,11 @@ With --gpus N (launched under torchrun) the layer runs expert-parallel: every
 rank routes its own 16384 tokens, rows travel to the rank that computes their
 expert segment and back (copy-engine writes into CUDA-IPC-mapped peer buffers,
 NCCL for the per-forward count all-gather), value = all ranks' tokens /
-max-over-ranks device time (weak scaling).
+max-over-ranks device time (weak scaling).  The headline placement is owner
+(E/N experts per GPU, BASELINE config 4's sharding) on uniform routing, the
+case the scaling target is defined for; the line also carries the other
+placement / routing combinations, the staged pipeline, and the same routing
+timed on one GPU in the same run (`one_gpu_same_routing.efficiency`).
 
 --impl reference times the reference's own implementation of the path on the
 box's host cores (the C restatement in oracle/, since the reference ships no
@@ -45,7 +49,9 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
+    p.add_argument("--routing", choices=["zipf", "uniform"], default=None,
+                   help="default: zipf on 1 GPU (config 3), uniform on several (config 4's "
+                        "4-experts-per-GPU sharding, the case the scaling target is set for)")
     p.add_argument("--tokens", type=int, default=T_DEFAULT)
     p.add_argument("--dtype", choices=["bf16", "tf32"], default="bf16")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -68,7 +74,11 @@ def parse():
     p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
                    help="only time b2_gemm_nt on one dense shape (bf16 operands), "
                         "e.g. for a profiler capture of the dense kernel")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.routing is None:
+        n = max(int(os.environ.get("WORLD_SIZE", "1")), args.gpus)
+        args.routing = "zipf" if n == 1 else "uniform"
+    return args
 
 
 def peaks():
@@ -498,6 +508,14 @@ def run_ours(args, rank, world, dev):
                 var[key] = {"value": r["value"], "ms_per_step": r["ms_per_step"],
                             "load": r["load"], "timeline_rank0_us": r["timeline"][0]}
             out["variants"] = var
+        # the same routing on one GPU (rank 0, the others wait): the weak-scaling
+        # efficiency of this line against its own single-GPU rate
+        if rank == 0:
+            one = time_layer(args, 0, 1, dev, args.ep_mode, args.routing)
+            out["one_gpu_same_routing"] = {
+                "value": one["value"], "ms_per_step": one["ms_per_step"],
+                "efficiency": value / (world * one["value"])}
+        dist.barrier()
     if "e2e" in head:
         out["e2e"] = head["e2e"]
     if not args.no_dense and rank == 0:
