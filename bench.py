@@ -633,7 +633,8 @@ def gemm_configs(args, dev, reps=20):
     ref = A.double() @ B.double().T
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     cfgs = ([("single", bn, 1) for bn in (64, 128, 256)] + [("pair", 256, 1)] +
-            [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)])
+            [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)] +
+            [("pairsplit", 256, sp) for sp in (2, 3, 4)])
     res = {"metric": "dense_gemm_configs", "M": M, "N": N, "K": Kd,
            "plan": list(gemm_plan(M, N, Kd, "bf16", sms)), "us": {}}
     for cfg in cfgs:

@@ -517,6 +517,9 @@ static b2_status gemm_nt_impl(const void *A, const void *B, float *C, int M, int
     if ((bn != 128 && bn != 256) || split < 2 || split > kSplitMax || split > kblocks)
       return B2_ERR_INVALID;
     plan = {false, bn, bn, split};
+  } else if (kind == 3) {
+    if (split < 2 || split > kPairSplitMax || split > kblocks) return B2_ERR_INVALID;
+    plan = {true, kBN, kBN / 2, split};
   } else if (kind >= 0) {
     return B2_ERR_INVALID;
   }
@@ -545,7 +548,7 @@ extern "C" b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, i
 extern "C" b2_status b2_gemm_nt_config(const void *A, const void *B, float *C, int M, int N,
                                        int K, int ldc, int dtype, int kind, int bn, int split,
                                        int *status, b2_stream stream_) {
-  if (kind < 0 || kind > 2) return B2_ERR_INVALID;
+  if (kind < 0 || kind > 3) return B2_ERR_INVALID;
   return gemm_nt_impl(A, B, C, M, N, K, ldc, dtype, kind, bn, split, status, stream_);
 }
 
@@ -556,7 +559,7 @@ extern "C" b2_status b2_gemm_plan(int M, int N, int K, int dtype, int sms, int *
     return B2_ERR_INVALID;
   const size_t es = dtype == B2_TF32 ? 4 : 2;
   const DensePlan p = plan_dense(M, N, sms, false, (int)(((size_t)K * es + kBKBytes - 1) / kBKBytes));
-  *kind = p.pair ? 1 : p.split > 1 ? 2 : 0;
+  *kind = p.pair ? (p.split > 1 ? 3 : 1) : p.split > 1 ? 2 : 0;
   *bn = p.bn;
   *split = p.split;
   return B2_OK;

@@ -17,6 +17,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
 #include "gemm_sm100_splitk.cuh"
+#include "gemm_sm100_pair_splitk.cuh"
 #include "host_tmap.h"
 #include "moe_kernels.cuh"
 
@@ -157,13 +158,14 @@ b2_status launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const G
 //          most that still run as one wave of co-resident clusters
 //          (max_clusters[s] = co-resident clusters of size s, from the
 //          device; kSplitMax caps it), each with >= 4 k-blocks;
-//   bn     else the widest single-CTA tile that gives every SM a tile, or 64.
+//   bn     else the single-CTA tile width (256, 128, 64) that needs the fewest
+//          waves, the wider one on a tie.
 // kb = 128-byte k-blocks of K (0: no split-K).
 struct DensePlan {
   bool pair;
   int bn;
   int b_box_rows;  // rows of the B tensor map's box
-  int split;       // CTAs per tile along K (1: no split)
+  int split;       // K-slices per tile (1: no split): CTAs, or CTA pairs when `pair`
 };
 
 constexpr int kSplitPlanMax = 6;  // clusters of 7-8 rarely all fit one wave on 148 SMs
@@ -188,9 +190,20 @@ inline DensePlan plan_dense(long long M, int N, int sms, bool swiglu, int kb = 0
   }
   if (swiglu) return {false, kBN, kBN, 1};
   if (tiles <= sms) return {false, 128, 128, 1};
-  for (int c : {256, 128})
-    if (mt * ((N + c - 1) / c) >= sms) return {false, c, c, 1};
-  return {false, 64, 64, 1};
+  // more 128-column tiles than SMs: the width with the fewest waves, the
+  // wider on a tie (at these sizes a 256-column tile costs ~1.1x a 128-column
+  // one, a second wave ~1.7x: 2048 x 2048 x 2048 took 24.4 us in 1.73 waves
+  // of 128-column tiles, 15.9 us in one wave of 256-column tiles)
+  int best = 256;
+  long long best_waves = (mt * ((N + 255) / 256) + sms - 1) / sms;
+  for (int c : {128, 64}) {
+    const long long w = (mt * ((N + c - 1) / c) + sms - 1) / sms;
+    if (w < best_waves) {
+      best = c;
+      best_waves = w;
+    }
+  }
+  return {false, best, best, 1};
 }
 
 // Co-resident clusters of each size 2..kSplitMax for the split-K kernels on
@@ -248,6 +261,47 @@ b2_status launch_gemm_splitk(const DensePlan &plan, const CUtensorMap &ta, const
   return B2_OK;
 }
 
+// Split-K over CTA pairs (gemm_sm100_pair_splitk.cuh): one cluster of
+// 2 * plan.split CTAs per 256 x 256 tile; tb's box has 128 rows.
+template <int EPI, bool TF32, typename TOut>
+b2_status launch_gemm_pair_splitk(const DensePlan &plan, const CUtensorMap &ta,
+                                  const CUtensorMap &tb, const GemmArgs &g, cudaStream_t s) {
+  if (plan.split < 2 || plan.split > kPairSplitMax) return B2_ERR_INVALID;
+  SplitArgs a{};
+  a.M = g.M;
+  a.N = g.N;
+  a.num_k_blocks = g.num_k_blocks;
+  a.splits = plan.split;
+  a.m_tiles = (g.M + kPairBM - 1) / kPairBM;
+  a.out = g.out;
+  a.ldo = g.ldo;
+  a.status = g.status;
+  a.accumulate = g.accumulate;
+  const int n_tiles = EPI == kEpiSwiGLU ? g.N / 128 : (g.N + kBN - 1) / kBN;
+  const int grid = a.m_tiles * n_tiles * 2 * plan.split;
+  auto kern = gemm_pair_splitk_kernel<EPI, TF32, TOut>;
+  static std::atomic<uint64_t> done{0};
+  B2_RETURN_IF(ensure_smem_limit(kern, pair_splitk_smem_bytes(), done));
+  if (grid <= 0) return B2_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = pair_splitk_smem_bytes();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2 * plan.split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+  B2_LAUNCHED();
+  return B2_OK;
+}
+
 // Launches a dense GEMM planned by plan_dense.  g.M, g.N, g.num_k_blocks,
 // g.out, g.ldo and g.status are set by the caller; tb's box has
 // plan.b_box_rows rows.
@@ -262,6 +316,7 @@ b2_status launch_dense(const DensePlan &plan, const CUtensorMap &ta, const CUten
   } else {
     g.num_n_tiles = (g.N + plan.bn - 1) / plan.bn;
   }
+  if (plan.pair && plan.split > 1) return launch_gemm_pair_splitk<EPI, TF32, TOut>(plan, ta, tb, g, s);
   if (plan.pair) {
     const int pairs = (int)std::min<long long>(sms / 2, mt_pair * g.num_n_tiles);
     return launch_gemm_pair<EPI, TF32, TOut>(ta, tb, g, pairs, s);

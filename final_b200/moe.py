@@ -144,7 +144,7 @@ class SparseMoeBlock:
             pass
 
 
-_KINDS = {"single": 0, "pair": 1, "splitk": 2}
+_KINDS = {"single": 0, "pair": 1, "splitk": 2, "pairsplit": 3}
 
 
 def gemm_nt(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
@@ -194,9 +194,10 @@ def launch_count() -> int:
 
 def gemm_plan(M: int, N: int, K: int, dtype: str = "bf16", sms: int = 148):
     """The kernel b2_gemm_nt picks for an M x N x K product on `sms` SMs:
-    ("single" | "pair" | "splitk", tile width, K splits).  Host only."""
+    ("single" | "pair" | "splitk" | "pairsplit", tile width, K splits).  Host
+    only."""
     lib = _lib.load()
     kind, bn, split = C.c_int(), C.c_int(), C.c_int()
     check(lib.b2_gemm_plan(M, N, K, _DT[dtype], sms, C.byref(kind), C.byref(bn), C.byref(split)),
           "b2_gemm_plan")
-    return ("single", "pair", "splitk")[kind.value], bn.value, split.value
+    return ("single", "pair", "splitk", "pairsplit")[kind.value], bn.value, split.value

@@ -176,15 +176,17 @@ b2_status b2_gemm_nt(const void *A, const void *B, float *C, int M, int N,
  * the planner (tuning sweeps, tests that reach every kernel on one shape):
  * kind 0 single-CTA tiles of width bn (64, 128, 256); 1 CTA pairs
  * (256 x 256); 2 split-K clusters of `split` CTAs (2..8) over 128 x bn tiles
- * (bn 128 or 256).  No counterpart in the reference. */
+ * (bn 128 or 256); 3 split-K clusters of `split` CTA pairs (2..4) over
+ * 256 x 256 tiles (bn ignored).  No counterpart in the reference. */
 b2_status b2_gemm_nt_config(const void *A, const void *B, float *C, int M, int N,
                             int K, int ldc, int dtype, int kind, int bn, int split,
                             int *status, b2_stream stream);
 
 /* The kernel configuration b2_gemm_nt uses for an M x N x K product on a
  * device with `sms` SMs (host only, no device call): *kind = 0 single-CTA
- * tiles, 1 CTA pairs (256 x 256), 2 split-K clusters; *bn = output tile
- * width; *split = CTAs per tile along K (1 unless kind == 2).  No
+ * tiles, 1 CTA pairs (256 x 256), 2 split-K clusters, 3 split-K clusters of
+ * CTA pairs; *bn = output tile width; *split = K-slices per tile (CTAs for
+ * kind 2, CTA pairs for kind 3; 1 otherwise).  No
  * counterpart in the reference, whose GEMM has one fixed 128 x 128 tiling
  * (src/layer.cu:9-141). */
 b2_status b2_gemm_plan(int M, int N, int K, int dtype, int sms, int *kind, int *bn,

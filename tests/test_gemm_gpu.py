@@ -38,7 +38,8 @@ SHAPES = [
 ]
 
 CONFIGS = ([("single", bn, 1) for bn in (64, 128, 256)] + [("pair", 256, 1)] +
-           [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)])
+           [("splitk", bn, sp) for bn in (128, 256) for sp in (2, 3, 4, 6, 8)] +
+           [("pairsplit", 256, sp) for sp in (2, 3, 4)])
 
 
 def _rel(a, b):
@@ -123,7 +124,7 @@ def test_gemm_invalid_args(cuda_dev):
 def test_every_configuration(cuda_dev, M, N, K, dtype):
     """Every kernel configuration (b2_gemm_nt_config) on the same operands:
     single-CTA 64/128/256-column tiles, CTA pairs, split-K with 128/256-column
-    tiles and 2..8 CTAs per cluster."""
+    tiles and 2..8 CTAs per cluster, split-K over 2..4 CTA pairs."""
     from final_b200 import gemm_nt
     g = torch.Generator(device=cuda_dev).manual_seed(M + 3 * N + 7 * K)
     A = torch.randn(M, K, device=cuda_dev, generator=g)
@@ -148,3 +149,20 @@ def test_splitk_is_deterministic(cuda_dev):
     c0 = gemm_nt(A, B, dtype="bf16")
     for _ in range(3):
         assert torch.equal(gemm_nt(A, B, dtype="bf16"), c0)
+
+
+@pytest.mark.parametrize("split", [2, 3, 4])
+def test_pair_splitk_is_deterministic(cuda_dev, split):
+    """Split-K over CTA pairs reduces its slices in a fixed order: repeated
+    calls give identical bits, on a shape whose last row and column tiles and
+    last k-block are partial."""
+    from final_b200 import gemm_nt
+    g = torch.Generator(device=cuda_dev).manual_seed(split)
+    A = torch.randn(300, 1000, device=cuda_dev, generator=g).to(torch.bfloat16)
+    B = (torch.randn(700, 1000, device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
+    ref = A.double() @ B.double().T
+    cfg = ("pairsplit", 256, split)
+    c0 = gemm_nt(A, B, dtype="bf16", config=cfg)
+    assert _rel(c0, ref) < 1e-4
+    for _ in range(3):
+        assert torch.equal(gemm_nt(A, B, dtype="bf16", config=cfg), c0)

@@ -13,7 +13,8 @@ from final_b200.moe import gemm_plan
     (512, 3072, 2048, ("single", 128, 1)),      # 96 tiles: one wave, no split
     (64, 2048, 7168, ("splitk", 128, 6)),       # decode MLP down projection
     (1, 4096, 2048, ("splitk", 128, 4)),
-    (1280, 2048, 2048, ("single", 128, 1)),
+    (1280, 2048, 2048, ("single", 256, 1)),     # 80 wide tiles in one wave, not 160 in two
+    (2048, 2048, 2048, ("single", 256, 1)),     # one wave: 15.9 us against 24.4 in two
     (128, 256, 64, ("single", 128, 1)),         # too little K to split
 ])
 def test_plan(M, N, K, want):
