@@ -38,6 +38,7 @@
 
 #include "../../include/b2moe_ep.h"
 #include "moe_internal.h"
+#include "ep_sched.cuh"
 
 using namespace b2;
 
@@ -281,15 +282,6 @@ struct EpComm {
   int refs = 1;
 };
 
-// A return chunk of the fused pipeline: consecutive W2 groups of one source,
-// receive-layout rows [row, row+rows) of out_recv, sent to rows [home,
-// home+rows) of the source's sout once its counter reaches `target`.
-struct ReturnChunk {
-  int src;
-  int64_t row, home, rows;
-  uint64_t target;  // epilogue-warp completions of the chunk's tiles
-};
-
 struct b2_ep {
   b2_moe *moe = nullptr;
   int world = 1, rank = 0, mode = 0, E = 0, n_wexp = 0;
@@ -315,6 +307,8 @@ struct b2_ep {
   unsigned long long *d_chunk_done = nullptr;  // [kMaxGroups]: return-chunk counters
   std::vector<ReturnChunk> chunks;     // return chunks of the last forward
   cudaEvent_t ev_w2go = nullptr, ev_dsp = nullptr;
+  cudaEvent_t ev_ag = nullptr;         // the count all-gather done (device side)
+  int *d_ngroups = nullptr;            // [2]: group counts of a schedule built on the GPU
   int32_t *d_fsched = nullptr, *h_fsched = nullptr;  // fused schedules: W1||W3, then W2
   int32_t *d_cnt_all = nullptr, *h_cnt_all = nullptr;
   int32_t *d_sched = nullptr, *h_sched = nullptr;  // per source: counts|offsets|mtile|group_b
@@ -330,12 +324,61 @@ struct b2_ep {
 static constexpr int kSchedInts = 4 * (kMaxGroups + 1);
 // a fused schedule: counts | C rows | m-tile prefix | expert | A rows | source | destination
 static constexpr int kFusedSchedInts = kPairSchedArrays * (kMaxGroups + 1);
+static_assert(kPairSchedArrays == kFusedSchedArrays && kSchedTileRows == kPairBM,
+              "the fused schedule's layout is the CTA-pair kernel's");
 
 // Sets every return-chunk counter far past any target (after W2 on the same
 // stream), so that a copy-engine wait on a counter always ends even if W2
 // aborted before counting all of its tiles.
 static __global__ void release_counters_kernel(unsigned long long *counters, int n) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) counters[i] = 1ull << 62;
+}
+
+// The fused pipeline's schedule in owner placement, built on the GPU from the
+// all-gathered count matrix as soon as the all-gather completes, so W1||W3
+// starts on the own rows without the host's round trip: W1||W3's and W2's
+// group lists and counts (owner_fused_schedule, the function the host runs
+// for its copies), the return-chunk counters reset, and the forward's
+// sequence number for the copy engines' flag writes.  One block; one thread
+// builds the lists from the matrix in shared memory.
+static __global__ void owner_plan_kernel(const int32_t *cnt_all, int G, int r, int E, int nt2,
+                                         int32_t *sched, int *ngroups,
+                                         unsigned long long *chunk_done, uint64_t *seq_out,
+                                         uint64_t seq) {
+  __shared__ int32_t c[B2_EP_MAX_WORLD * kMaxExperts];
+  for (int i = threadIdx.x; i < G * E; i += blockDim.x) c[i] = cnt_all[i];
+  for (int i = threadIdx.x; i < kMaxGroups; i += blockDim.x) chunk_done[i] = 0ull;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int mt = 0;
+    ngroups[0] = owner_fused_schedule(G, r, E, c, false, 0, kMaxGroups + 1, sched, &mt, nullptr,
+                                      nullptr);
+    ngroups[1] = owner_fused_schedule(G, r, E, c, true, nt2, kMaxGroups + 1,
+                                      sched + kPairSchedArrays * (kMaxGroups + 1), &mt, nullptr,
+                                      nullptr);
+    *seq_out = seq;
+  }
+}
+
+// Bounded wait until every rank d in `mask` has raised this rank's return
+// flag (flags[ret0 + d] >= target), one thread per rank; gives up after
+// timeout_ns recording kDevTimeoutPeer.  The ranks come as a bit mask (the
+// world is at most 64), so nothing has to be uploaded for it.
+static __global__ void wait_return_flags_kernel(const volatile uint64_t *flags, int ret0,
+                                                uint64_t mask, uint64_t target,
+                                                uint64_t timeout_ns, int *status) {
+  const int d = threadIdx.x;
+  if (d < 64 && ((mask >> d) & 1)) {
+    const uint64_t t0 = globaltimer();
+    while (flags[ret0 + d] < target) {
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicCAS(status, 0, (int)kDevTimeoutPeer);
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+  __threadfence_system();
 }
 
 // cuStreamWaitValue64 / cuDeviceGetAttribute from the driver, looked up once
@@ -494,6 +537,7 @@ extern "C" b2_status b2_ep_destroy(b2_ep *ep) {
   if (ep->ev_cnt) cudaEventDestroy(ep->ev_cnt);
   if (ep->ev_w2go) cudaEventDestroy(ep->ev_w2go);
   if (ep->ev_dsp) cudaEventDestroy(ep->ev_dsp);
+  if (ep->ev_ag) cudaEventDestroy(ep->ev_ag);
   if (ep->st_d) cudaStreamDestroy(ep->st_d);
   if (ep->st_r) cudaStreamDestroy(ep->st_r);
   if (ep->h_cnt_all) cudaFreeHost(ep->h_cnt_all);
@@ -567,6 +611,7 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
   if ((st = moe_alloc(m, (void **)&ep->d_chunk_done, sizeof(unsigned long long) * kMaxGroups)) !=
       B2_OK)
     return fail(st);
+  if ((st = moe_alloc(m, (void **)&ep->d_ngroups, sizeof(int) * 2)) != B2_OK) return fail(st);
   ep->fused_ok = stream_wait64_supported();
   if (!ep->fused_ok) ep->pipeline = B2_EP_PIPE_STAGED;
   if (cudaMallocHost(&ep->h_cnt_all, sizeof(int32_t) * world * kMaxExperts) != cudaSuccess ||
@@ -589,7 +634,8 @@ b2_status b2::ep_create_impl(const b2_moe_desc *desc, int world, int rank,
       cudaEventCreateWithFlags(&ep->ev_scan, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->ev_cnt, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->ev_w2go, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->ev_dsp, cudaEventDisableTiming) != cudaSuccess)
+      cudaEventCreateWithFlags(&ep->ev_dsp, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->ev_ag, cudaEventDisableTiming) != cudaSuccess)
     return fail(B2_ERR_CUDA);
   ep->ev_out.resize(world, nullptr);
   for (int k = 0; k < world; ++k)
@@ -718,8 +764,6 @@ static int fill_sched(const b2_ep_plan &p, int src, bool self_rows, int64_t self
 // source the groups keep the plan's expert order.  Returns the number of
 // groups; *mtiles the 256-row tiles; `chunks` (may be null) the return chunks
 // with their counter targets for W2's n_tiles output tiles per row block.
-constexpr int64_t kReturnChunkRows = 4096;
-
 static int fill_fused(int G, int r, const b2_ep_plan *plans, bool w2, int n_tiles, int32_t *h,
                       int *mtiles, std::vector<ReturnChunk> *chunks) {
   constexpr int N1 = kMaxGroups + 1;
@@ -787,48 +831,25 @@ extern "C" b2_status b2_ep_fused_schedule(int world, int rank, int num_experts, 
   std::vector<b2_ep_plan> plans(world);
   for (int q = 0; q < world; ++q)
     B2_RETURN_IF(b2_ep_plan_compute(world, q, num_experts, mode, counts, &plans[q]));
+  if (mode == B2_EP_OWNER) {
+    *groups = owner_fused_schedule(world, rank, num_experts, counts, w2 != 0, 1, kMaxGroups + 1,
+                                   sched, mtiles, nullptr, nullptr);
+    return *groups < 0 ? B2_ERR_INVALID : B2_OK;
+  }
   *groups = fill_fused(world, rank, plans.data(), w2 != 0, 1, sched, mtiles, nullptr);
   return B2_OK;
 }
 
-// The fused exchange + expert GEMMs (B2_EP_PIPE_FUSED), from the uploaded
-// plan to the moment every source has returned this rank's rows.
-static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
-                             const std::function<b2_status(int)> &tl) {
+// W1||W3 of one fused launch over every source's rows.  ngroups_dev: the
+// group count on the GPU (a schedule built there) instead of n1.
+static b2_status launch_fused_w13(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns, int n1,
+                                  int mt1, const int *ngroups_dev) {
   b2_moe *m = ep->moe;
-  const int G = ep->world, r = ep->rank, H = m->d.hidden, Ip = m->Ip;
+  const int G = ep->world, H = m->d.hidden, Ip = m->Ip;
   const bool f = m->tf32;
-  const b2_ep_plan &p = ep->plans[r];
-  const size_t rb = (f ? 4 : 2) * (size_t)H;
-  const int nt2 = (H + kBN - 1) / kBN;
-  int mt1 = 0, mt2 = 0;
-  const int n1 = fill_fused(G, r, ep->plans.data(), false, 0, ep->h_fsched, &mt1, nullptr);
-  const int n2 = fill_fused(G, r, ep->plans.data(), true, nt2, ep->h_fsched + kFusedSchedInts,
-                            &mt2, &ep->chunks);
-  const int nchunks = (int)ep->chunks.size();
-  B2_CUDA(cudaMemcpyAsync(ep->d_fsched, ep->h_fsched, sizeof(int32_t) * 2 * kFusedSchedInts,
-                          cudaMemcpyHostToDevice, s));
-  B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
-  int nwait_ret = 0;
-  for (int d = 0; d < G; ++d)
-    if (d != r && p.send_cnt[d] > 0) ep->h_wait_idx[G + nwait_ret++] = kFlagReturn * G + d;
-  if (nwait_ret > 0)
-    B2_CUDA(cudaMemcpyAsync(ep->d_wait_idx + G, ep->h_wait_idx + G, sizeof(int) * nwait_ret,
-                            cudaMemcpyHostToDevice, s));
-  B2_CUDA(cudaEventRecord(ep->ev_ready, s));
-  // every return chunk's counter starts at zero (before W1||W3, so that W1||W3
-  // and W2 follow each other directly and overlap by programmatic launch)
-  if (nchunks > 0)
-    B2_CUDA(cudaMemsetAsync(ep->d_chunk_done, 0, sizeof(unsigned long long) * nchunks, s));
-  B2_CUDA(cudaEventRecord(ep->ev_w2go, s));
-  B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
-  prof_mark(m, s);  // expert GEMMs start
-
   constexpr int N1 = kMaxGroups + 1;
-  const int32_t *d1 = ep->d_fsched, *d2 = ep->d_fsched + kFusedSchedInts;
+  const int32_t *d1 = ep->d_fsched;
   const int max_pairs = m->sms / 2;
-  // every wait of the W1||W3 launch may last as long as a source's flag wait
-  const uint64_t wait_ns = timeout_ns + kWaitTimeoutNs;
   GemmArgs a1{};
   a1.counts = d1;
   a1.offsets = d1 + N1;
@@ -837,6 +858,7 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   a1.a_offsets = d1 + 4 * N1;
   a1.group_src = d1 + 5 * N1;
   a1.num_groups = n1;
+  a1.num_groups_dev = ngroups_dev;
   a1.b_rows_per_group = 2 * Ip;
   a1.N = Ip;
   a1.num_n_tiles = Ip / 128;
@@ -847,21 +869,89 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   a1.flags = ep->flags + kFlagDispatch * G;
   a1.flag_target = ep->seq;
   a1.c_rows = ep->inter_rows;
-  a1.wait_ns = wait_ns;
-  const int pairs1 = (int)std::min<long long>(max_pairs, (long long)mt1 * a1.num_n_tiles);
-  if (n1 > 0) {
-    if (f)
-      B2_RETURN_IF((launch_gemm_pair<kEpiSwiGLU, true, float>(m->tm_x, m->tm_w13_half, a1, pairs1,
-                                                              s, &ep->tm_recv)));
-    else
-      B2_RETURN_IF((launch_gemm_pair<kEpiSwiGLU, false, __nv_bfloat16>(
-          m->tm_x, m->tm_w13_half, a1, pairs1, s, &ep->tm_recv)));
+  // every wait of the launch may last as long as a source's flag wait
+  a1.wait_ns = timeout_ns + kWaitTimeoutNs;
+  // a schedule built on the GPU: as many pairs as the device has (extra pairs
+  // find no tile and leave at once)
+  const int pairs1 =
+      ngroups_dev ? max_pairs
+                  : (int)std::min<long long>(max_pairs, (long long)mt1 * a1.num_n_tiles);
+  if (!ngroups_dev && n1 == 0) return B2_OK;
+  if (f)
+    return launch_gemm_pair<kEpiSwiGLU, true, float>(m->tm_x, m->tm_w13_half, a1, pairs1, s,
+                                                     &ep->tm_recv);
+  return launch_gemm_pair<kEpiSwiGLU, false, __nv_bfloat16>(m->tm_x, m->tm_w13_half, a1, pairs1,
+                                                            s, &ep->tm_recv);
+}
+
+// Owner placement, fused pipeline: once the count all-gather has completed
+// on the GPU, one small kernel builds this rank's schedule (owner_plan_kernel)
+// and W1||W3 starts on the own rows -- the host has not seen the counts yet.
+static b2_status fused_w13_device_plan(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
+                                       const std::function<b2_status(int)> &tl) {
+  b2_moe *m = ep->moe;
+  const int nt2 = (m->d.hidden + kBN - 1) / kBN;
+  B2_CUDA(cudaStreamWaitEvent(s, ep->ev_ag, 0));
+  owner_plan_kernel<<<1, 128, 0, s>>>(ep->d_cnt_all, ep->world, ep->rank, ep->E, nt2,
+                                      ep->d_fsched, ep->d_ngroups, ep->d_chunk_done, ep->d_seq,
+                                      ep->seq);
+  B2_LAUNCHED();
+  // schedule, chunk counters and sequence number are in place
+  B2_CUDA(cudaEventRecord(ep->ev_w2go, s));
+  B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
+  return launch_fused_w13(ep, s, timeout_ns, 0, 0, ep->d_ngroups);
+}
+
+// The fused exchange + expert GEMMs (B2_EP_PIPE_FUSED), from the host's plan
+// to the moment every source has returned this rank's rows.  dplan: the
+// schedule was built on the GPU and W1||W3 launched already
+// (fused_w13_device_plan); the host builds the same lists for its copies.
+static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
+                             const std::function<b2_status(int)> &tl, bool dplan) {
+  b2_moe *m = ep->moe;
+  const int G = ep->world, r = ep->rank, H = m->d.hidden, Ip = m->Ip;
+  const bool f = m->tf32;
+  const b2_ep_plan &p = ep->plans[r];
+  const size_t rb = (f ? 4 : 2) * (size_t)H;
+  const int nt2 = (H + kBN - 1) / kBN;
+  int mt1 = 0, mt2 = 0, n1 = 0, n2 = 0;
+  if (ep->mode == B2_EP_OWNER) {
+    int nch = 0;
+    ep->chunks.resize(kMaxGroups);
+    n1 = owner_fused_schedule(G, r, ep->E, ep->h_cnt_all, false, 0, kMaxGroups + 1,
+                              ep->h_fsched, &mt1, nullptr, nullptr);
+    n2 = owner_fused_schedule(G, r, ep->E, ep->h_cnt_all, true, nt2, kMaxGroups + 1,
+                              ep->h_fsched + kFusedSchedInts, &mt2, ep->chunks.data(), &nch);
+    if (n1 < 0 || n2 < 0) return B2_ERR_INVALID;
+    ep->chunks.resize(nch);
+  } else {
+    n1 = fill_fused(G, r, ep->plans.data(), false, 0, ep->h_fsched, &mt1, nullptr);
+    n2 = fill_fused(G, r, ep->plans.data(), true, nt2, ep->h_fsched + kFusedSchedInts, &mt2,
+                    &ep->chunks);
   }
-  // dispatch on the copy engine (enqueued after the GEMM, which starts on the
-  // own rows meanwhile): step k pushes the rows for rank r+k into its receive
-  // buffer, then our sequence number into its flag slot
+  const int nchunks = (int)ep->chunks.size();
+  uint64_t ret_mask = 0;  // ranks that return rows of ours
+  for (int d = 0; d < G; ++d)
+    if (d != r && p.send_cnt[d] > 0) ret_mask |= 1ull << d;
+  if (!dplan) {
+    B2_CUDA(cudaMemcpyAsync(ep->d_fsched, ep->h_fsched, sizeof(int32_t) * 2 * kFusedSchedInts,
+                            cudaMemcpyHostToDevice, s));
+    B2_CUDA(cudaMemcpyAsync(ep->d_seq, ep->h_seq, sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+    // every return chunk's counter starts at zero (before W1||W3, so that
+    // W1||W3 and W2 follow each other directly and overlap by programmatic
+    // launch)
+    if (nchunks > 0)
+      B2_CUDA(cudaMemsetAsync(ep->d_chunk_done, 0, sizeof(unsigned long long) * nchunks, s));
+    B2_CUDA(cudaEventRecord(ep->ev_w2go, s));
+    B2_RETURN_IF(tl(B2_EP_TL_PLANNED));
+    B2_RETURN_IF(launch_fused_w13(ep, s, timeout_ns, n1, mt1, nullptr));
+  }
+  // dispatch on the copy engine (the GEMM is running on the own rows
+  // meanwhile): step k pushes the rows for rank r+k into its receive buffer,
+  // then our sequence number into its flag slot.  ev_w2go follows the scatter
+  // and the sequence number's update.
   const char *sx = reinterpret_cast<const char *>(m->sorted_x);
-  B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_ready, 0));
+  B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_w2go, 0));
   for (int k = 1; k < G; ++k) {
     const int to = (r + k) % G;
     if (p.send_cnt[to])
@@ -875,6 +965,8 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   prof_mark(m, s);  // W2 starts
 
   // W2: own rows into sout, a peer's rows into out_recv (local stores only)
+  constexpr int N1 = kMaxGroups + 1;
+  const int32_t *d2 = ep->d_fsched + kFusedSchedInts;
   GemmArgs a2{};
   a2.counts = d2;
   a2.offsets = d2 + N1;
@@ -886,6 +978,7 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   a2.chunk_done = ep->d_chunk_done;
   a2.out_ptrs = ep->d_out_ptrs;
   a2.num_groups = n2;
+  a2.num_groups_dev = dplan ? ep->d_ngroups + 1 : nullptr;
   a2.b_rows_per_group = H;
   a2.N = H;
   a2.num_n_tiles = nt2;
@@ -896,7 +989,7 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
   // rows of the larger destination: out_recv (a peer's rows, receive layout)
   // or sout (own rows, expert-sorted)
   a2.c_rows = std::max<int64_t>(ep->cap_rows, (int64_t)m->d.max_tokens * m->d.top_k);
-  const int pairs2 = (int)std::min<long long>(max_pairs, (long long)mt2 * a2.num_n_tiles);
+  const int pairs2 = (int)std::min<long long>(m->sms / 2, (long long)mt2 * a2.num_n_tiles);
   if (n2 > 0) {
     if (f)
       B2_RETURN_IF(
@@ -939,9 +1032,9 @@ static b2_status fused_gemms(b2_ep *ep, cudaStream_t s, uint64_t timeout_ns,
       B2_CUDA(cudaMemcpyAsync(ep->peer_flags[ch.src] + kFlagReturn * G + r, ep->d_seq,
                               sizeof(uint64_t), cudaMemcpyDeviceToDevice, ep->st_r));
   }
-  if (nwait_ret > 0) {
-    wait_flags_kernel<<<1, 32 * ((nwait_ret + 31) / 32), 0, s>>>(
-        ep->flags, ep->d_wait_idx + G, nwait_ret, ep->seq, timeout_ns, m->status);
+  if (ret_mask) {
+    wait_return_flags_kernel<<<1, 64, 0, s>>>(ep->flags, kFlagReturn * G, ret_mask, ep->seq,
+                                             timeout_ns, m->status);
     B2_LAUNCHED();
   }
   if (G > 1) {
@@ -997,12 +1090,21 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
   B2_CUDA(cudaEventRecord(ep->ev_scan, s));
   B2_CUDA(cudaStreamWaitEvent(ep->st_d, ep->ev_scan, 0));
   B2_NCCL(nccl().AllGather(m->counts, ep->d_cnt_all, E, ncclInt32, ep->cm->comm, ep->st_d));
+  B2_CUDA(cudaEventRecord(ep->ev_ag, ep->st_d));
   B2_CUDA(cudaMemcpyAsync(ep->h_cnt_all, ep->d_cnt_all, sizeof(int32_t) * G * E,
                           cudaMemcpyDeviceToHost, ep->st_d));
   B2_CUDA(cudaEventRecord(ep->ev_cnt, ep->st_d));
   if (T > 0) B2_RETURN_IF(moe_scatter_stage(m, x, T, s));
   prof_mark(m, s);  // exchange + expert GEMMs start
   B2_RETURN_IF(tl(B2_EP_TL_SCATTERED));
+  // fused pipeline, owner placement: W1||W3 is scheduled on the GPU and
+  // launched now; the host's round trip below only sizes the copies
+  const bool dplan = ep->pipeline == B2_EP_PIPE_FUSED && ep->fused_ok && ep->mode == B2_EP_OWNER;
+  if (dplan) {
+    ep->seq += 1;
+    *ep->h_seq = ep->seq;
+    B2_RETURN_IF(fused_w13_device_plan(ep, s, timeout_ns, tl));
+  }
   const auto h0 = std::chrono::steady_clock::now();
   {
     cudaEvent_t ev = ep->ev_cnt;
@@ -1013,10 +1115,12 @@ b2_status b2::ep_forward_impl(b2_ep *ep, const float *x, float *y, int T, cudaSt
     B2_RETURN_IF(b2_ep_plan_compute(G, q, E, ep->mode, ep->h_cnt_all, &ep->plans[q]));
   const b2_ep_plan &p = ep->plans[r];
   if (p.recv_rows > ep->cap_rows) return B2_ERR_CAPACITY;
-  ep->seq += 1;
-  *ep->h_seq = ep->seq;
+  if (!dplan) {
+    ep->seq += 1;
+    *ep->h_seq = ep->seq;
+  }
   if (ep->pipeline == B2_EP_PIPE_FUSED && ep->fused_ok) {
-    B2_RETURN_IF(fused_gemms(ep, s, timeout_ns, tl));
+    B2_RETURN_IF(fused_gemms(ep, s, timeout_ns, tl, dplan));
     // 6. local k-ordered combine
     if (T > 0) {
       B2_RETURN_IF(moe_combine_stage(m, y, T, s, accumulate));

@@ -53,6 +53,7 @@ struct GemmArgs {
   const int *mtile_offsets;  // grouped: exclusive prefix of ceil(count/128), [G+1]
   const int *group_b;        // grouped, optional: B block of each group (default: the group index)
   int num_groups;            // grouped: G (<= kMaxGroups); dense: 0
+  const int *num_groups_dev; // CTA-pair grouped schedule built on the GPU: G read here
   int b_rows_per_group;      // grouped: rows of B per group
   int M;                     // dense rows
   int N;                     // output columns (SwiGLU: gated output columns)

@@ -51,16 +51,16 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmArgs &g
                                                      const int *s_grp, const int *s_aoff,
                                                      const int *s_src, const int *s_dst,
                                                      const int *s_chunk, int out_tile_cols,
-                                                     int crank) {
+                                                     int crank, int ngroups) {
   TileInfo t;
   const int NT = g.num_n_tiles;
   t.src = -1;
   t.dst = 0;
   t.chunk = -1;
-  if (g.num_groups > 0) {
+  if (ngroups > 0) {
     const int gm = tile / NT;
     const int n = tile - gm * NT;
-    int lo = 0, hi = g.num_groups;  // s_mt[lo] <= gm < s_mt[hi]
+    int lo = 0, hi = ngroups;  // s_mt[lo] <= gm < s_mt[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
       if (s_mt[mid] <= gm) lo = mid; else hi = mid;
@@ -152,10 +152,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   pdl_wait();
   pdl_trigger();
-  if (g.num_groups > 0) {
-    for (int i = threadIdx.x; i <= g.num_groups; i += blockDim.x) {
+  // grouped schedule: the group count is a launch parameter, or (when the
+  // schedule itself was built on the GPU) read from device memory; a count
+  // outside [0, kMaxGroups] runs no tile
+  int ngroups = g.num_groups;
+  if (g.num_groups_dev) {
+    ngroups = *g.num_groups_dev;
+    if (ngroups < 0 || ngroups > kMaxGroups) ngroups = 0;
+  }
+  const bool grouped = g.num_groups > 0 || g.num_groups_dev != nullptr;
+  if (grouped) {
+    for (int i = threadIdx.x; i <= ngroups; i += blockDim.x) {
       s_mt[i] = g.mtile_offsets[i];
-      if (i < g.num_groups) {
+      if (i < ngroups) {
         s_off[i] = g.offsets[i];
         s_cnt[i] = g.counts[i];
         s_grp[i] = g.group_b ? g.group_b[i] : i;
@@ -172,8 +181,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   const int NT = g.num_n_tiles;
-  const int total_tiles = g.num_groups > 0
-                              ? s_mt[g.num_groups] * NT
+  const int total_tiles = grouped
+                              ? s_mt[ngroups] * NT
                               : ((g.M + kPairBM - 1) / kPairBM) * NT;
   constexpr int out_tile_cols = (EPI == kEpiSwiGLU) ? kBN / 2 : kBN;
   const int KB = g.num_k_blocks;
@@ -189,7 +198,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint64_t arrived = 0;  // sources whose rows this producer has seen published
       for (int tile = pair; tile < total_tiles; tile += npairs) {
         const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
-                                            s_dst, s_chunk, out_tile_cols, (int)crank);
+                                            s_dst, s_chunk, out_tile_cols, (int)crank,
+                                            grouped ? ngroups : 0);
         const CUtensorMap *ta = &tmA;
         if (t.src >= 0) {
           ta = &tmA2;
@@ -292,7 +302,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_par = 0;
     for (int tile = pair; tile < total_tiles; tile += npairs) {
       const TileInfo t = decode_pair_tile(tile, g, s_mt, s_off, s_cnt, s_grp, s_aoff, s_src,
-                                          s_dst, s_chunk, out_tile_cols, (int)crank);
+                                          s_dst, s_chunk, out_tile_cols, (int)crank,
+                                            grouped ? ngroups : 0);
       if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, g.status, kDevTimeoutEpilogue,
                      wait_ns))
         break;
