@@ -442,6 +442,7 @@ def time_layer(args, rank, world, dev, mode, routing, pipeline="fused", e2e=Fals
 
 
 def run_ours(args, rank, world, dev):
+    import torch.distributed as dist
     T = args.tokens
     keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline
     head = time_layer(args, rank, world, dev, args.ep_mode, args.routing, e2e=not args.no_e2e,
@@ -518,7 +519,9 @@ def run_ours(args, rank, world, dev):
         dist.barrier()
     if "e2e" in head:
         out["e2e"] = head["e2e"]
-    if not args.no_dense and rank == 0:
+    if not args.no_dense and world == 1:
+        # single-GPU measurements (with several ranks the others would wait
+        # for rank 0 in a barrier meanwhile)
         out["dense_gemm_sweep"] = dense_sweep(dev)
         out["dense_mlp"] = mlp_bench(dev)
     if not args.no_model:
