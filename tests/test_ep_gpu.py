@@ -2,9 +2,9 @@
 
 Every rank's output must be bit-identical to the single-GPU layer's output for
 the same tokens: rows meet the same expert in the same kernels, and the
-combine order does not change.  The 2-rank test needs two GPUs and is skipped
-on a one-GPU box (the host-side exchange logic is covered on CPU by
-tests/test_ep_plan.py)."""
+combine order does not change.  The several-rank tests run one process per
+GPU at 2, 4 and 8 ranks and skip the rank counts the box has too few GPUs for
+(the host-side exchange logic is covered on CPU by tests/test_ep_plan.py)."""
 import os
 import socket
 
@@ -91,32 +91,40 @@ def _rank_main(rank, world, port, mode, q, pipeline="fused"):
         dist.destroy_process_group()
 
 
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("pipeline", ["fused", "staged"])
 @pytest.mark.parametrize("mode", ["owner", "balanced"])
-def test_ep_two_ranks_match_single_gpu(cuda_dev, mode, pipeline):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs (host-side exchange logic is tested on CPU)")
+def test_ep_ranks_match_single_gpu(cuda_dev, mode, pipeline, world):
+    """world ranks (one per GPU) over the same 512 tokens: the concatenated
+    outputs are bit-identical to the single-GPU layer's, with 32 / world
+    experts per GPU in owner placement."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs (host-side exchange logic is tested on CPU)")
     import torch.multiprocessing as mp
     inp = build_case("zipf")
     want = _single_gpu_y(inp, cuda_dev).numpy()
-    with socket.socket() as sk:
-        sk.bind(("127.0.0.1", 0))
-        port = sk.getsockname()[1]
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, mode, q, pipeline))
-             for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, mode, q, pipeline))
+             for r in range(world)]
     for p in procs:
         p.start()
     got = {}
-    for _ in range(2):
+    for _ in range(world):
         r, y, status, rows = q.get(timeout=300)
         assert status == 0
         got[r] = y
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    y = np.concatenate([got[0], got[1]])
+    y = np.concatenate([got[r] for r in range(world)])
     assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
 
 
@@ -176,14 +184,16 @@ def _config4_rank_main(rank, world, port, mode, routing, outdir, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("routing", ["uniform", "zipf"])
-def test_ep_two_ranks_config4_owner(cuda_dev, routing, tmp_path):
-    """Config 4 sharded as 16 experts per GPU on 2 GPUs (owner placement),
-    32768 tokens per rank: every rank's y is bit-identical to the single-GPU
-    layer's y for the same tokens (the single-GPU layer itself is checked
-    against the oracle at this size by test_moe_gpu.test_moe_config4_one_gpu)."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs (host-side exchange logic is tested on CPU)")
+def test_ep_ranks_config4_owner(cuda_dev, routing, world, tmp_path):
+    """Config 4 (65536 tokens) sharded as 32 / world experts per GPU (owner
+    placement: 16, 8, 4 experts per GPU on 2, 4, 8 GPUs), 65536 / world tokens
+    per rank: every rank's y is bit-identical to the single-GPU layer's y for
+    the same tokens (the single-GPU layer itself is checked against the oracle
+    at this size by test_moe_gpu.test_moe_config4_one_gpu)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs (host-side exchange logic is tested on CPU)")
     import torch.multiprocessing as mp
     from final_b200 import SparseMoeBlock
     x, gate, bias, w1, w2, w3 = _config4_inputs(routing, cuda_dev)
@@ -194,17 +204,16 @@ def test_ep_two_ranks_config4_owner(cuda_dev, routing, tmp_path):
     torch.cuda.synchronize()
     layer.close()
     torch.cuda.empty_cache()
-    with socket.socket() as sk:
-        sk.bind(("127.0.0.1", 0))
-        port = sk.getsockname()[1]
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_config4_rank_main,
-                         args=(r, 2, port, "owner", routing, str(tmp_path), q)) for r in range(2)]
+                         args=(r, world, port, "owner", routing, str(tmp_path), q))
+             for r in range(world)]
     for p in procs:
         p.start()
     got, rows = {}, {}
-    for _ in range(2):
+    for _ in range(world):
         r, path, status, nrows, same = q.get(timeout=600)
         assert status == 0
         assert same, f"rank {r}: second forward differs"
@@ -213,6 +222,6 @@ def test_ep_two_ranks_config4_owner(cuda_dev, routing, tmp_path):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert rows[0] + rows[1] == x.shape[0] * 4
-    y = np.concatenate([got[0], got[1]])
+    assert sum(rows.values()) == x.shape[0] * 4
+    y = np.concatenate([got[r] for r in range(world)])
     assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
