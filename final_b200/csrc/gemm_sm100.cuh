@@ -47,6 +47,18 @@ constexpr int kEpiStageBytes = 4 * kEpiWarpBytes;  // 4 epilogue warps
 
 enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1 };
 
+// SwiGLU of one accumulator pair, silu(g) * u, with the sigmoid written as
+// 0.5 + 0.5 tanh(g / 2) on the hardware tanh: one MUFU operation and no
+// branch, so a chunk's 32 outputs pipeline (an IEEE division's slow-path
+// branch serialised them).  The approximate tanh's error (about 2^-11) is
+// below the bf16 rounding of the stored intermediate.  Every GEMM kernel's
+// SwiGLU epilogue uses this function, so they all give the same bits.
+__device__ __forceinline__ float swiglu(float g, float u) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+  return g * fmaf(0.5f, t, 0.5f) * u;
+}
+
 struct GemmArgs {
   const int *counts;         // grouped: rows per group
   const int *offsets;        // grouped: first row of each group in A / C
@@ -451,10 +463,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld_wait();
           float h[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gv = __uint_as_float(gr[i]);
-            h[i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(ur[i]);
-          }
+          for (int i = 0; i < 32; ++i) h[i] = swiglu(__uint_as_float(gr[i]), __uint_as_float(ur[i]));
           store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
                       lane);
         }

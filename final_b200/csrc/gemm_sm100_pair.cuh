@@ -329,10 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld_wait();
           float h[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gv = __uint_as_float(gr[i]);
-            h[i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(ur[i]);
-          }
+          for (int i = 0; i < 32; ++i) h[i] = swiglu(__uint_as_float(gr[i]), __uint_as_float(ur[i]));
           store_chunk(stage, h, out + c * 32, g.ldo, rows_valid, t.cols_valid - c * 32, vec_ok,
                       lane);
         }

@@ -318,9 +318,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               ga.x += gv[j].x; ga.y += gv[j].y; ga.z += gv[j].z; ga.w += gv[j].w;
               ua.x += uv[j].x; ua.y += uv[j].y; ua.z += uv[j].z; ua.w += uv[j].w;
             }
-          store4(out + (long long)grow * g.ldo + gcol, ga.x / (1.0f + __expf(-ga.x)) * ua.x,
-                 ga.y / (1.0f + __expf(-ga.y)) * ua.y, ga.z / (1.0f + __expf(-ga.z)) * ua.z,
-                 ga.w / (1.0f + __expf(-ga.w)) * ua.w, vec_ok, g.N - gcol);
+          store4(out + (long long)grow * g.ldo + gcol, swiglu(ga.x, ua.x), swiglu(ga.y, ua.y),
+                 swiglu(ga.z, ua.z), swiglu(ga.w, ua.w), vec_ok, g.N - gcol);
         }
       }
     }
