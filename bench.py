@@ -391,7 +391,7 @@ def time_layer(args, rank, world, dev, mode, routing, pipeline="fused", e2e=Fals
         s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
         ev = lambda: torch.cuda.Event()
 
-        def pipelined(steps):
+        def pipelined(steps, with_layer=True):
             done_c = [None, None]   # layer of step i finished reading xd / writing yd
             done_o = [None, None]   # D2H of step i finished reading yd
             for i in range(steps):
@@ -404,7 +404,8 @@ def time_layer(args, rank, world, dev, mode, routing, pipeline="fused", e2e=Fals
                 stream.wait_event(e_in)
                 if done_o[b] is not None:
                     stream.wait_event(done_o[b])
-                fwd(xd[b], yd[b])
+                if with_layer:
+                    fwd(xd[b], yd[b])
                 e_c = ev(); e_c.record(stream); done_c[b] = e_c
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(e_c)
@@ -429,9 +430,32 @@ def time_layer(args, rank, world, dev, mode, routing, pipeline="fused", e2e=Fals
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = t.item()
+        # the same pipeline with the layer left out: the time the two copy
+        # streams alone need for these bytes on this box's PCIe link, the
+        # bound of the end-to-end figure
+        pipelined(3, with_layer=False)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record(stream)
+        s_in.wait_stream(stream)
+        pipelined(args.steps, with_layer=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        cms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([cms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            cms = t.item()
         res["e2e"] = {"value": T * args.steps * world / (ems / 1e3), "unit": "tokens/s",
                       "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
                       "ms_per_step": ems / args.steps,
+                      "copy_bound": {
+                          "ms_per_step": cms / args.steps,
+                          "value": T * args.steps * world / (cms / 1e3),
+                          "h2d_d2h_gbs_each_way": T * H * 4 * args.steps / (cms / 1e3) / 1e9,
+                          "frac": cms / ems,
+                          "how": "the same pipeline and copies with the layer left out"},
                       "how": "pinned host x -> device, layer, device y -> pinned host every "
                              "step; copies overlap neighbouring steps' layers on two copy "
                              "streams"}
