@@ -71,6 +71,9 @@ def parse():
                    help="with --gpus > 1, skip the other placements / routings / pipeline")
     p.add_argument("--gemm-configs", type=int, nargs=3, metavar=("M", "N", "K"),
                    help="time every dense-GEMM kernel configuration on one shape (bf16)")
+    p.add_argument("--gemm-launches", type=int, nargs=3, metavar=("M", "N", "K"),
+                   help="launch six dense-GEMM configurations and torch.mm four times "
+                        "each, eagerly (for a one-pass ncu launch list)")
     p.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"),
                    help="only time b2_gemm_nt on one dense shape (bf16 operands), "
                         "e.g. for a profiler capture of the dense kernel")
@@ -691,6 +694,31 @@ def gemm_configs(args, dev, reps=20):
     return res
 
 
+def gemm_launches(args, dev):
+    """Four eager launches of each of six kernel configurations of
+    b2_gemm_nt_config, then four of torch.mm (cuBLAS) on the same bf16
+    operands: run under `ncu --metrics gpu__time_duration.sum`, the launch
+    list gives each kernel's own duration next to cuBLAS's."""
+    import torch
+    from final_b200 import gemm_nt, to_bf16
+    M, N, Kd = args.gemm_launches
+    g = torch.Generator(device=dev).manual_seed(2)
+    A = to_bf16(torch.randn(M, Kd, device=dev, generator=g))
+    B = to_bf16(torch.randn(N, Kd, device=dev, generator=g) * 0.02)
+    C = torch.empty(M, N, device=dev)
+    cfgs = [("single", 64, 1), ("single", 128, 1), ("pair", 256, 1), ("splitk", 128, 2),
+            ("splitk", 128, 4), ("pairsplit", 256, 2)]
+    for cfg in cfgs:
+        for _ in range(4):
+            gemm_nt(A, B, out=C, config=cfg)
+        torch.cuda.synchronize()
+    for _ in range(4):
+        torch.mm(A, B.t())
+    torch.cuda.synchronize()
+    return {"metric": "dense_gemm_launches", "M": M, "N": N, "K": Kd,
+            "configs": ["/".join(map(str, c)) for c in cfgs] + ["torch.mm"], "launches_each": 4}
+
+
 def mlp_bench(dev, T=16384, Hd=2048, Id=7168, reps=10):
     """Dense SwiGLU MLP of the layers without experts (I = 7168) over T tokens
     on the same GEMM core: tokens/s and TFLOP/s (6*T*H*I FLOP per forward)."""
@@ -1002,6 +1030,9 @@ def main():
         return 0
     if args.gemm_configs:
         print(json.dumps(gemm_configs(args, dev)), flush=True)
+        return 0
+    if args.gemm_launches:
+        print(json.dumps(gemm_launches(args, dev)), flush=True)
         return 0
     if args.model_only:
         fm = model_bench(dev, steps=args.steps, warmup=args.warmup, rank=rank, world=world)
