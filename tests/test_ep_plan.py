@@ -1,7 +1,7 @@
 """Expert-parallel host logic on CPU: the exchange plan (b2_ep_plan_compute,
 the C ABI of include/b2moe_ep.h) and the whole dispatch -> expert FFN ->
 return -> combine dataflow, emulated with the CPU oracle, single-process and
-as two gloo ranks.  The expert-parallel result must equal the single-rank
+as two and four gloo ranks.  The expert-parallel result must equal the single-rank
 result bit for bit: every row meets the same expert and the combine order is
 unchanged."""
 import os
@@ -390,8 +390,12 @@ def _gloo_rank(rank, world, port, mode, result_q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("mode", ["owner", "balanced"])
-def test_ep_two_gloo_ranks_match_single_rank(oracle, mode):
+def test_ep_gloo_ranks_match_single_rank(oracle, mode, world):
+    """world gloo ranks (processes) run the exchange plan with real
+    collectives: count all-gather, rows to their owners, results back; the
+    concatenated y equals the single-rank layer's bit for bit."""
     import socket
     import torch.multiprocessing as mp
     from moe_cases import build_case
@@ -403,17 +407,17 @@ def test_ep_two_gloo_ranks_match_single_rank(oracle, mode):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
-    for _ in range(2):
-        r, y, _rows = q.get(timeout=120)
+    for _ in range(world):
+        r, y, _rows = q.get(timeout=180)
         got[r] = y
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    y = np.concatenate([got[0], got[1]])
+    y = np.concatenate([got[r] for r in range(world)])
     assert np.array_equal(y.view(np.uint32), ref["y"].view(np.uint32))
 
 
